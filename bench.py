@@ -1,0 +1,522 @@
+"""Benchmark of the quantized-linear hot path on B200 (one JSON line on rank 0).
+
+Headline workload (BASELINE config 3 at M = 1): the Qwen2.5-7B decode linear-layer sweep,
+28 layers x {qkv 3584->4608, o 3584->3584, gate_up 3584->37888, down 18944->3584}, W4A16
+group-128 AWQ weights with random codes (q, z uniform in [0, 15], scales uniform(0.002, 0.02)),
+repacked once by the awq_repack kernel. A "step" is one pass over all 112 layers. At N GPUs
+the layers are tensor-parallel (column-split qkv/gate_up, row-split o/down + NCCL all-reduce
+of the fp16 partials), so the total work is fixed and ``scaling`` is "strong".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--m M] [--impl ours|reference]
+
+Metric: achieved W4A16 HBM GB/s, i.e. algorithmic bytes of every layer in the step
+(N*K/2 + (K/G)*N*2 + (K/G)*N/2 + M*K*2 + M*N*2 per layer, the reference's formula in
+tokenforge/bench/micro.py:82-86, summed over ranks) divided by the device time of the step,
+max over ranks. The step streams 3.4 GB of weights, far more than the 126 MB L2, so no layer's
+weights are cache-resident when it runs (no separate L2 flush).
+The same line carries the W4A16 GEMM TFLOP/s at M = 1024 (config 2, gate_up + down).
+
+``--impl reference`` times the reference's CPU path (dequantize + fp32 matmul, w4a16_torch of
+tokenforge/kernels/reference.py:24-32) through the oracle's C port on all host cores, on one
+decoder layer of the same workload per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+HIDDEN, INTER, LAYERS, G = 3584, 18944, 28, 128
+# name, N, K, parallel kind
+LAYER_SHAPES = [
+    ("qkv", 4608, HIDDEN, "column"),
+    ("o", HIDDEN, HIDDEN, "row"),
+    ("gate_up", 2 * INTER, HIDDEN, "column"),
+    ("down", HIDDEN, INTER, "row"),
+]
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def algorithmic_bytes(m: int, n: int, k: int, g: int = G) -> int:
+    return n * k // 2 + (k // g) * n * 2 + (k // g) * n // 2 + m * k * 2 + m * n * 2
+
+
+def peaks() -> tuple[dict[str, float], str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"])}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5,
+                ).stdout.strip()
+                if out:
+                    self.samples.append([v.strip() for v in out.split(",")])
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self) -> ClockSampler:
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict[str, object]:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 3 + i and s[3 + i].lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(self.samples),
+        }
+
+
+# ----------------------------------------------------------------------------- workload
+
+
+class DecodeSweep:
+    """This rank's shards of the 28-layer sweep plus the C-ABI argument tuples of a step."""
+
+    def __init__(self, m: int, rank: int, world: int, device: torch.device, seed: int = 0) -> None:
+        from tokenforge_b200 import _lib, tp
+        from tokenforge_b200.pack import W4A16Weights
+
+        self.m, self.rank, self.world, self.device = m, rank, world, device
+        self.lib = _lib.lib()
+        gen = torch.Generator(device=device).manual_seed(seed * 7919 + rank)
+        self.layers: list[list[tuple[str, W4A16Weights, tuple[int, int]]]] = []
+        self.bytes_per_step = 0  # this rank's algorithmic bytes
+        self.shard_shapes: dict[str, tuple[int, int]] = {}
+        for _ in range(LAYERS):
+            row = []
+            for name, n, k, kind in LAYER_SHAPES:
+                if kind == "column":
+                    n0, n1 = tp.column_bounds(n, world)[rank]
+                    nn, kk, bounds = n1 - n0, k, (n0, n1)
+                else:
+                    k0, k1 = tp.row_bounds(k, G, world)[rank]
+                    nn, kk, bounds = n, k1 - k0, (k0, k1)
+                qweight = torch.randint(-(2**31), 2**31 - 1, (kk, nn // 8), generator=gen,
+                                        dtype=torch.int32, device=device)
+                qzeros = torch.randint(-(2**31), 2**31 - 1, (kk // G, nn // 8), generator=gen,
+                                       dtype=torch.int32, device=device)
+                scales = (torch.rand((kk // G, nn), generator=gen, device=device) * 0.018
+                          + 0.002).to(torch.float16)
+                qweight_t = torch.ops.tokenforge.awq_repack(qweight)
+                del qweight
+                row.append((name, W4A16Weights(qweight_t, scales, qzeros, G), bounds))
+                self.bytes_per_step += algorithmic_bytes(m, nn, kk)
+                self.shard_shapes[name] = (nn, kk)
+            self.layers.append(row)
+        xg = torch.Generator(device=device).manual_seed(seed + 17)
+        self.x_h = torch.randn((m, HIDDEN), generator=xg, device=device).to(torch.float16)
+        self.x_o = torch.randn((m, HIDDEN), generator=xg, device=device).to(torch.float16)
+        self.x_d = torch.randn((m, INTER), generator=xg, device=device).to(torch.float16)
+        self.y = {name: torch.empty((m, self.shard_shapes[name][0]), dtype=torch.float16,
+                                    device=device) for name, *_ in LAYER_SHAPES}
+        ws = max(int(self.lib.tf_w4a16_workspace_bytes(m, nn, kk, G))
+                 for nn, kk in self.shard_shapes.values())
+        self.ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
+        self.ws_bytes = ws
+        self.calls: list[tuple[str, tuple]] = []
+        for row in self.layers:
+            for name, w, bounds in row:
+                if name in ("qkv", "gate_up"):
+                    x, ldx = self.x_h, HIDDEN
+                    xp = x.data_ptr()
+                else:
+                    x = self.x_o if name == "o" else self.x_d
+                    ldx = x.stride(0)
+                    xp = x.data_ptr() + bounds[0] * 2  # this rank's K slice
+                y = self.y[name]
+                args = (xp, m, w.k, ldx, w.qweight_t.data_ptr(), w.scales.data_ptr(),
+                        w.qzeros.data_ptr(), None, w.n, G, y.data_ptr(), w.n,
+                        self.ws.data_ptr(), self.ws_bytes)
+                self.calls.append((name, args))
+        self.launches_per_step = 0
+        for name, (nn, kk) in self.shard_shapes.items():
+            out = (ctypes.c_int32 * 8)()
+            self.lib.tf_launch_plan(m, nn, kk, G, ctypes.addressof(out))
+            self.launches_per_step += LAYERS * (1 + (1 if out[4] > 1 else 0))
+
+    def step(self, only: str | None = None, allreduce: bool = True) -> None:
+        import torch.distributed as dist
+
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        fn = self.lib.tf_w4a16_linear
+        for name, args in self.calls:
+            if only is not None and name != only:
+                continue
+            st = fn(*args, stream)
+            if st != 0:
+                raise RuntimeError(f"tf_w4a16_linear({name}) failed with status {st}")
+            if allreduce and self.world > 1 and name in ("o", "down"):
+                dist.all_reduce(self.y[name])
+
+
+def capture(fn, device: torch.device) -> torch.cuda.CUDAGraph:  # type: ignore[no-untyped-def]
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize(device)
+    return g
+
+
+def time_graph(g: torch.cuda.CUDAGraph, reps: int, device: torch.device, barrier=None) -> float:  # type: ignore[no-untyped-def]
+    """Milliseconds for ``reps`` back-to-back replays, timed with CUDA events."""
+    torch.cuda.synchronize(device)
+    if barrier:
+        barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end)
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+
+def cpu_baseline(m: int, reps: int = 1) -> dict[str, object]:
+    """The oracle's C port of the reference CPU path on one decoder layer (all host cores)."""
+    from oracle import oracle
+
+    cores = os.cpu_count() or 1
+    gen = torch.Generator().manual_seed(5)
+    tensors, total = [], 0
+    for _, n, k, _ in LAYER_SHAPES:
+        qw = torch.randint(-(2**31), 2**31 - 1, (n, k // 8), generator=gen, dtype=torch.int32)
+        z = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32)
+        s = (torch.rand((k // G, n), generator=gen) * 0.018 + 0.002).to(torch.float16)
+        x = torch.randn((m, k), generator=gen).to(torch.float16)
+        tensors.append((x, qw, s, z))
+        total += algorithmic_bytes(m, n, k)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for x, qw, s, z in tensors:
+            oracle.w4a16_cpu(x, qw, s, z, G, threads=cores)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {
+        "value": round(total / sec / 1e9, 4),
+        "unit": "GB/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": f"one decoder layer (qkv, o, gate_up, down) at M={m}, {total} algorithmic "
+                  f"bytes, median of {reps}",
+        "seconds_per_sample": round(sec, 4),
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    t_all = time.perf_counter()
+    for _ in range(args.warmup):
+        cpu_baseline(args.m, reps=1)
+    samples = [cpu_baseline(args.m, reps=1) for _ in range(args.steps)]
+    value = statistics.median(float(s["value"]) for s in samples)
+    sec = statistics.median(float(s["seconds_per_sample"]) for s in samples)
+    cb = dict(samples[0])
+    cb["value"] = value
+    cb.pop("seconds_per_sample", None)
+    line = {
+        "impl": "reference",
+        "metric": "W4A16 GEMV HBM GB/s at M=1 (Qwen2.5-7B decode sweep)",
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int4xfp16->fp32",
+        "data": "synthetic",
+        "config": {"workload": f"config3 decode sweep sample: one decoder layer at M={args.m}",
+                   "m": args.m, "group_size": G},
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(time.perf_counter() - t_all, 2),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GEMM (config 2)
+
+
+def gemm_metric(device: torch.device, m: int, steps: int, warmup: int, pk: dict, src: str) -> dict:
+    from tokenforge_b200 import _lib
+    from tokenforge_b200.config import launch_plan
+
+    lib = _lib.lib()
+    gen = torch.Generator(device=device).manual_seed(3)
+    calls, flops, names = [], 0, []
+    keep = []
+    for name, n, k, _ in (LAYER_SHAPES[2], LAYER_SHAPES[3]):
+        qweight = torch.randint(-(2**31), 2**31 - 1, (k, n // 8), generator=gen, dtype=torch.int32, device=device)
+        qz = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32, device=device)
+        s = (torch.rand((k // G, n), generator=gen, device=device) * 0.018 + 0.002).to(torch.float16)
+        qt = torch.ops.tokenforge.awq_repack(qweight)
+        x = torch.randn((m, k), generator=gen, device=device).to(torch.float16)
+        y = torch.empty((m, n), dtype=torch.float16, device=device)
+        ws_b = int(lib.tf_w4a16_workspace_bytes(m, n, k, G))
+        ws = torch.empty(max(ws_b, 16), dtype=torch.uint8, device=device)
+        keep += [qt, qz, s, x, y, ws]
+        calls.append((x.data_ptr(), m, k, k, qt.data_ptr(), s.data_ptr(), qz.data_ptr(), None, n, G,
+                      y.data_ptr(), n, ws.data_ptr(), ws_b))
+        flops += 2 * m * n * k
+        names.append(f"{name} {launch_plan(m, n, k, G).kernel}")
+
+    def step() -> None:
+        st = torch.cuda.current_stream(device).cuda_stream
+        for a in calls:
+            rc = lib.tf_w4a16_linear(*a, st)
+            if rc != 0:
+                raise RuntimeError(f"gemm failed: {rc}")
+
+    g = capture(step, device)
+    for _ in range(warmup):
+        g.replay()
+    ms = time_graph(g, steps, device) / steps
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {
+        "metric": f"W4A16 GEMM TFLOP/s at M={m} (Qwen2.5-7B gate_up + down, config 2)",
+        "value": round(tflops, 2),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms, 4),
+        "kernels": names,
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops"], 4),
+                     "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
+    }
+
+
+# ----------------------------------------------------------------------------- main
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--gemm-m", type=int, default=1024)
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warmup must be >= 3", file=sys.stderr)
+        sys.exit(2)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch.distributed as dist
+
+    import tokenforge_b200.ops  # noqa: F401
+    from tokenforge_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    if world != args.gpus:
+        print(f"--gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    _lib.set_launch_flags(0 if args.no_pdl else _lib.TF_LAUNCH_PDL)
+    pk, src = peaks()
+
+    sweep = DecodeSweep(args.m, rank, world, device)
+    if world > 1:
+        warm = torch.ones(1, device=device)
+        dist.all_reduce(warm)
+    barrier = (lambda: dist.barrier(device_ids=[local])) if world > 1 else None
+
+    graph = capture(sweep.step, device)
+    for _ in range(args.warmup):
+        graph.replay()
+    with ClockSampler(local) as clocks:
+        ms_total = time_graph(graph, args.steps, device, barrier)
+    ms = ms_total / args.steps
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    b = torch.tensor([sweep.bytes_per_step], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+    ms_max = float(t.item())
+    total_bytes = float(b.item())
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+
+    # Roofline of the dominant kernel (the W4A16 GEMV): each layer type's 28 launches replayed
+    # back to back as a graph, timed with CUDA events; algorithmic bytes / mean launch time.
+    per_kind = {}
+    kind_bytes = kind_ms = 0.0
+    for name, *_ in LAYER_SHAPES:
+        g = capture(lambda name=name: sweep.step(only=name, allreduce=False), device)
+        for _ in range(3):
+            g.replay()
+        reps = max(3, args.steps // 2)
+        kms = time_graph(g, reps, device) / reps / LAYERS
+        nn, kk = sweep.shard_shapes[name]
+        kb = algorithmic_bytes(args.m, nn, kk)
+        per_kind[name] = {"n": nn, "k": kk, "us_per_launch": round(kms * 1e3, 3),
+                          "gbs": round(kb / (kms * 1e-3) / 1e9, 1)}
+        kind_bytes += kb * LAYERS
+        kind_ms += kms * LAYERS
+        del g
+    achieved = kind_bytes / (kind_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "gemv_dram_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_step_tp1")
+
+    # End to end through the C ABI with host buffers: pinned H2D of the step's activations,
+    # 112 eager tf_w4a16_linear calls (plus the all-reduces), D2H of the step's last output.
+    h_in = [torch.empty_like(x, device="cpu").pin_memory() for x in (sweep.x_h, sweep.x_o, sweep.x_d)]
+    for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
+        hbuf.copy_(x.cpu())
+    h_out = torch.empty_like(sweep.y["down"], device="cpu").pin_memory()
+    h2d = sum(h.numel() * h.element_size() for h in h_in)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step() -> None:
+        for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
+            x.copy_(hbuf, non_blocking=True)
+        sweep.step()
+        h_out.copy_(sweep.y["down"], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if barrier:
+        barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
+    e2e_ms = torch.tensor([max(e0.elapsed_time(e1) / args.steps, wall_ms)], device=device,
+                          dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = total_bytes / (float(e2e_ms.item()) * 1e-3) / 1e9
+
+    gemm = None
+    if world == 1 and not args.skip_gemm:
+        gemm = gemm_metric(device, args.gemm_m, max(3, args.steps // 2), 3, pk, src)
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.m, reps=1)
+
+    if rank == 0:
+        line = {
+            "metric": "W4A16 GEMV HBM GB/s at M=1 (Qwen2.5-7B decode sweep, 28 layers)"
+                      if args.m == 1 else f"W4A16 GEMV HBM GB/s at M={args.m} (Qwen2.5-7B decode sweep)",
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "int4xfp16->fp32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"config3 decode sweep: 28 layers x (qkv, o, gate_up, down), M={args.m}, "
+                            f"TP={world}, CUDA-graph replay",
+                "m": args.m, "group_size": G, "tp": world,
+                "parallelism": f"tp{world}" + (" (NCCL all-reduce after o/down)" if world > 1 else ""),
+                "l2": "inputs larger than L2 (3.4 GB of weights streamed per step)",
+                "pdl": not args.no_pdl,
+                "bytes_per_step": int(total_bytes),
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                "peak_source": f"{src} hbm_gbs",
+                "kernel": "w4a16_mma_kernel (GEMV, M<=8)",
+                "per_layer": per_kind,
+            },
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(float(e2e_ms.item()), 4),
+                    "path": "tf_w4a16_linear via ctypes, eager, pinned host buffers"},
+            "gpu_launches": sweep.launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "gemm": gemm,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

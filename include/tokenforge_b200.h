@@ -1,0 +1,171 @@
+/*
+ * tokenforge_b200.h — C ABI of the B200 (sm_100a) quantized-linear backend.
+ *
+ * These entry points are the native boundary underneath the reference's custom ops
+ * (`torch.ops.tokenforge.*`, reference file tokenforge/kernels/ops.py). Every function takes
+ * plain device pointers, element counts and a CUDA stream handle (`cudaStream_t` passed as
+ * `void*`; NULL is the legacy default stream), enqueues its work on that stream and returns
+ * a status code without synchronising. No function reads tensor values on the host, so each
+ * one can be recorded into a CUDA graph.
+ *
+ * Data types on the boundary:
+ *   fp16 tensors are `uint16_t` bit patterns (IEEE binary16);
+ *   e4m3 tensors are `uint8_t` bit patterns (OCP float8 e4m3fn, the torch.float8_e4m3fn codes);
+ *   packed int4 tensors are `int32_t` words, eight 4-bit values per word in the AWQ nibble
+ *   interleave (nibble i holds column/row offset (0,2,4,6,1,3,5,7)[i]).
+ *
+ * Tensor layouts (row-major, innermost dimension last):
+ *   AWQ checkpoint  qweight   int32 [K, N/8]     packed along N
+ *                   qzeros    int32 [K/G, N/8]   packed along N
+ *                   scales    fp16  [K/G, N]
+ *   kernel layout   qweight_t int32 [N, K/8]     packed along K, same nibble interleave
+ *   activations     x         fp16  [M, K] with row stride ldx (elements), unit stride along K
+ *   output          y         fp16  [M, N] with row stride ldy (elements)
+ *
+ * Alignment contract: every pointer to a 16-byte-vectorised operand (x, qweight_t, y, the
+ * rmsnorm rows) must be 16-byte aligned and its row stride a multiple of 8 fp16 elements;
+ * otherwise the call returns TF_ERR_ALIGNMENT and enqueues nothing (the Python layer copies
+ * misaligned activations to an aligned buffer first).
+ */
+#ifndef TOKENFORGE_B200_H
+#define TOKENFORGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TF_API __attribute__((visibility("default")))
+#else
+#define TF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. 0 is success; everything else enqueued no work unless stated. */
+enum {
+  TF_OK = 0,
+  TF_ERR_INVALID_ARG = 1,   /* a size, group size or pointer argument is invalid */
+  TF_ERR_ALIGNMENT = 2,     /* a vectorised operand is not 16-byte aligned */
+  TF_ERR_WORKSPACE = 3,     /* workspace pointer missing or smaller than required */
+  TF_ERR_UNSUPPORTED = 4,   /* shape outside what the kernels implement */
+  TF_ERR_CUDA = 5,          /* a CUDA runtime call failed (see tf_last_cuda_error) */
+  TF_ERR_NO_DEVICE = 6,     /* the current device is not compute capability 10.0 */
+  TF_ERR_TOO_LARGE = 7      /* a size exceeds a fixed capacity of the entry point */
+};
+
+/* Human-readable text of a status code (static storage). */
+TF_API const char* tf_status_string(int status);
+
+/* The last CUDA runtime error seen by this library on the calling thread (cudaError_t value). */
+TF_API int tf_last_cuda_error(void);
+
+/* ABI version of this header; bumped on any signature change. */
+TF_API int tf_abi_version(void);
+
+/* Process-wide launch flags.
+ * TF_LAUNCH_PDL: W4A16 linear kernels are launched with programmatic dependent launch and
+ *   start streaming their weights before the preceding kernel on the stream has finished
+ *   (activations are read, and outputs written, only after it has). Set it only when no
+ *   kernel enqueued directly before a W4A16 call on the same stream writes that call's
+ *   qweight_t, scales or qzeros. Off by default. */
+#define TF_LAUNCH_PDL 1u
+TF_API void tf_set_launch_flags(uint32_t flags);
+TF_API uint32_t tf_get_launch_flags(void);
+
+/* ------------------------------------------------------------------------- AWQ repack
+ * Replaces repack_awq_to_tf (reference tokenforge/kernels/pack.py:141-143), the load-time
+ * conversion inside pack_awq (pack.py:171-181).
+ * qweight: int32 [K, N/8] AWQ layout  ->  qweight_t: int32 [N, K/8] kernel layout.
+ * Bit-exact: output word (n, j) holds the eight values of column n at rows 8j..8j+7 in the
+ * same nibble interleave. Requires K % 8 == 0, N % 8 == 0. */
+TF_API int tf_awq_repack(const int32_t* qweight, int64_t K, int64_t N, int32_t* qweight_t,
+                  void* stream);
+
+/* Inverse, repack_tf_to_awq (pack.py:146-148): qweight_t [N, K/8] -> qweight [K, N/8]. */
+TF_API int tf_awq_unrepack(const int32_t* qweight_t, int64_t N, int64_t K, int32_t* qweight,
+                    void* stream);
+
+/* Nibble codec of the AWQ interleave (pack_int4 / unpack_int4, pack.py:42-67).
+ * unpack: packed int32 [n_words] -> int32 values [8 * n_words] in [0, 15], value 8w + j taken
+ *         from nibble (j % 2) * 4 + j / 2 of word w.
+ * pack:   int32 values [8 * n_words] -> packed int32 [n_words]; only the low 4 bits of each
+ *         value are used (range checking belongs to the caller, as in pack.py:45-47). */
+TF_API int tf_unpack_int4(const int32_t* packed, int64_t n_words, int32_t* values, void* stream);
+TF_API int tf_pack_int4(const int32_t* values, int64_t n_words, int32_t* packed, void* stream);
+
+/* ------------------------------------------------------------------------- dequant
+ * Replaces the w4a16_dequant op (ops.py:110-120; Triton kernel triton/w4a16.py:118-146;
+ * torch rule dequantize_tf pack.py:189-194).
+ * out[n, k] = fp16(q[n, k] - z[k/G, n]) * s[k/G, n], one fp16 rounding: bit-exact.
+ * out: fp16 [N, K] (nn.Linear.weight layout). group_size in {32, 64, 128}. */
+TF_API int tf_w4a16_dequant(const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                     int64_t N, int64_t K, int32_t group_size, uint16_t* out, void* stream);
+
+/* ------------------------------------------------------------------------- W4A16 linear
+ * y[m, n] = sum_k x[m, k] * dequant(W)[n, k] (+ bias[n]), fp32 accumulation, fp16 output.
+ *
+ * tf_w4a16_gemv replaces the planned extension entry `_C.w4a16_gemv(x2, qweight_t, scales,
+ * qzeros, bias, group_size)` named at ops.py:86-88 (decode, M = 1..8).
+ * tf_w4a16_gemm covers M >= 9 (prefill) with the sm_100a tensor-core kernel.
+ * tf_w4a16_linear is the per-call dispatch of the w4a16_linear op (ops.py:48-94) through the
+ * fixed per-M-bucket launch table (replacing autotune.lookup, autotune.py:190-193).
+ *
+ * bias may be NULL. Workspace: tf_w4a16_workspace_bytes(M, N, K, group_size) bytes of device
+ * memory (may be 0, then workspace may be NULL); contents need not be initialised; it must
+ * not be used by another call that runs concurrently. */
+TF_API size_t tf_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_size);
+
+TF_API int tf_w4a16_gemv(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                  const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                  const uint16_t* bias, int64_t N, int32_t group_size,
+                  uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+TF_API int tf_w4a16_gemm(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                  const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                  const uint16_t* bias, int64_t N, int32_t group_size,
+                  uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+TF_API int tf_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                    const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                    const uint16_t* bias, int64_t N, int32_t group_size,
+                    uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Launch-table introspection (replaces config.default_config / GemmConfig, config.py:23-92).
+ * Writes the launch chosen for (M, N, K, G) into out[0..7]:
+ *   {kernel (0 = gemv, 1 = mma gemm, 2 = tcgen05 gemm), m_bucket, tile_n, warps_k, split_k,
+ *    tile_m, grid_x, grid_y}. Returns TF_OK or TF_ERR_INVALID_ARG. */
+TF_API int tf_launch_plan(int64_t M, int64_t N, int64_t K, int32_t group_size, int32_t* out);
+
+/* ------------------------------------------------------------------------- RMSNorm + FP8
+ * Replaces rmsnorm_fp8_quant (ops.py:130-146; Triton kernel triton/rmsnorm_fp8.py:44-73;
+ * torch rule reference.py:35-56).
+ * Per row t: y = fp16(x * (1 / sqrt_rn(mean(x^2) + eps))) * weight (fp16 product), then
+ *   dynamic (static_scale == NULL): scale[t] = max(amax|y| / 448, 1 / (448 * 512)), written
+ *                                   to scale_out[t];
+ *   static: scale = *static_scale (device pointer to one fp32), scale_out is not written;
+ *   q = e4m3_rne_satfinite(clamp(y / scale, -448, 448)).
+ * x: fp16 [T, H] row stride ldx; weight: fp16 [H]; q: e4m3 [T, H] contiguous. */
+TF_API int tf_rmsnorm_fp8_quant(const uint16_t* x, int64_t T, int64_t H, int64_t ldx,
+                         const uint16_t* weight, float eps, const float* static_scale,
+                         uint8_t* q, float* scale_out, void* stream);
+
+/* fp32 -> e4m3 (round to nearest even, saturating to +-448, NaN stays NaN), the exact cast
+ * the quantizer uses. Mirrors the probe kernel of the reference's midpoint test
+ * (tests/numerics/test_rmsnorm_fp8.py:22-27). */
+TF_API int tf_cast_e4m3(const float* in, int64_t n, uint8_t* out, void* stream);
+
+/* Device-side status word written by kernels whose waits are bounded (the tcgen05 GEMM):
+ * 0 = no error. Reading it synchronises the current device; resetting writes 0. */
+TF_API int tf_device_error(int* out_code);
+TF_API int tf_reset_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOKENFORGE_B200_H */

@@ -1,0 +1,119 @@
+"""The C ABI surface of the kernel library, checked without a GPU: the shared object loads,
+exports every function ``include/tokenforge_b200.h`` declares, and its host-only entry points
+(status strings, launch planning, argument validation) behave as documented."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tokenforge_b200 import _lib
+from tokenforge_b200.config import launch_plan, m_bucket, workspace_bytes
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "tokenforge_b200.h"
+
+
+def _declared() -> list[str]:
+    return re.findall(r"^TF_API [\w\s\*]+?\b(tf_\w+)\(", HEADER.read_text(), flags=re.M)
+
+
+def test_header_declares_the_boundary() -> None:
+    names = set(_declared())
+    for required in ("tf_awq_repack", "tf_w4a16_dequant", "tf_w4a16_gemv", "tf_w4a16_gemm",
+                     "tf_w4a16_linear", "tf_rmsnorm_fp8_quant", "tf_launch_plan"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    lib = _lib.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_declared()) <= set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version() -> None:
+    assert _lib.status_string(0) == "ok"
+    assert "aligned" in _lib.status_string(_lib.TF_ERR_ALIGNMENT)
+    assert _lib.status_string(999) == "unknown status"
+    assert _lib.lib().tf_abi_version() == 1
+
+
+def test_launch_flags_roundtrip() -> None:
+    old = _lib.get_launch_flags()
+    try:
+        _lib.set_launch_flags(_lib.TF_LAUNCH_PDL)
+        assert _lib.get_launch_flags() == _lib.TF_LAUNCH_PDL
+    finally:
+        _lib.set_launch_flags(old)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8])
+def test_decode_sizes_use_the_gemv(m: int) -> None:
+    plan = launch_plan(m, 4608, 3584, 128)
+    assert plan.kernel == "gemv"
+    assert plan.m_bucket == m_bucket(m)
+    assert plan.tile_m == 8
+
+
+@pytest.mark.parametrize("m", [9, 16, 64, 129, 1024, 4096, 5000])
+def test_prefill_sizes_use_a_gemm(m: int) -> None:
+    plan = launch_plan(m, 37888, 3584, 128)
+    assert plan.kernel in ("tcgen05_gemm", "mma_gemm")
+
+
+@pytest.mark.parametrize(("n", "k"), [(4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944),
+                                      (200, 256), (1000, 1024), (896, 4864), (1152, 896)])
+def test_plan_covers_every_k_block_once(n: int, k: int) -> None:
+    plan = launch_plan(1, n, k, 128)
+    kblocks = -(-k // 128)
+    assert plan.warps_k in (1, 2, 4, 8)
+    assert plan.grid_x * (8 // plan.warps_k) * 16 >= n
+    assert 1 <= plan.split_k <= 8
+    per = -(-kblocks // plan.split_k)
+    assert (plan.split_k - 1) * per < kblocks <= plan.split_k * per  # no empty split
+    ws = workspace_bytes(1, n, k, 128)
+    assert ws == (plan.split_k * n * 4 if plan.split_k > 1 else 0)
+
+
+def test_plan_is_deterministic() -> None:
+    assert launch_plan(3, 37888, 3584, 128) == launch_plan(3, 37888, 3584, 128)
+
+
+def test_plan_rejects_bad_shapes() -> None:
+    with pytest.raises(ValueError, match="no launch"):
+        launch_plan(1, 4608, 3584, 256)
+    with pytest.raises(ValueError, match="no launch"):
+        launch_plan(1, 4604, 3584, 128)
+    with pytest.raises(ValueError, match="no launch"):
+        launch_plan(0, 4608, 3584, 128)
+
+
+def test_entry_points_validate_before_touching_the_device() -> None:
+    lib = _lib.lib()
+    # Invalid group size / shapes are rejected on the host with no launch.
+    st = lib.tf_w4a16_linear(None, 1, 3584, 3584, None, None, None, None, 4608, 96, None, 4608,
+                             None, 0, None)
+    assert st == _lib.TF_ERR_INVALID_ARG
+    st = lib.tf_w4a16_gemv(None, 1, 3584, 3584, None, None, None, None, 4604, 128, None, 4604,
+                           None, 0, None)
+    assert st == _lib.TF_ERR_INVALID_ARG
+    # M == 0 is a no-op.
+    st = lib.tf_w4a16_linear(None, 0, 3584, 3584, None, None, None, None, 4608, 128, None, 4608,
+                             None, 0, None)
+    assert st == _lib.TF_OK
+    # Misaligned activations are refused (the Python layer copies them first).
+    st = lib.tf_w4a16_linear(2, 1, 256, 256, 16, 16, 16, None, 64, 128, 16, 64, None, 0, None)
+    assert st == _lib.TF_ERR_ALIGNMENT
+    # A split-K launch without its workspace is refused.
+    assert workspace_bytes(1, 896, 4864, 128) > 0
+    st = lib.tf_w4a16_linear(16, 1, 4864, 4864, 16, 16, 16, None, 896, 128, 16, 896, None, 0, None)
+    assert st == _lib.TF_ERR_WORKSPACE
+    st = lib.tf_awq_repack(None, 12, 8, None, None)
+    assert st == _lib.TF_ERR_INVALID_ARG
+    st = lib.tf_rmsnorm_fp8_quant(None, 0, 896, 896, None, ctypes.c_float(1e-6), None, None, None, None)
+    assert st == _lib.TF_OK
+    st = lib.tf_w4a16_dequant(None, None, None, 64, 256, 48, None, None)
+    assert st == _lib.TF_ERR_INVALID_ARG

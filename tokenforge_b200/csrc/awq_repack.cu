@@ -1,0 +1,176 @@
+// AWQ repack: qweight [K, N/8] (packed along N) -> qweight_t [N, K/8] (packed along K).
+//
+// Semantics follow repack_awq_to_tf (reference tokenforge/kernels/pack.py:141-143): the
+// logical int4 matrix is transposed and re-packed with the same nibble interleave
+// (nibble i of a word holds offset AWQ_ORDER[i] = (0,2,4,6,1,3,5,7)[i], pack.py:32).
+//
+// One thread owns an 8x8 block of int4 values per step: eight input words (rows k0..k0+7 of
+// one column word) become eight output words (columns 8c..8c+7, one row word k0/8). Because
+// both layouts use the same interleave, the block is a plain 8x8 nibble transpose once the
+// input words are taken in AWQ_ORDER and the output words are written in AWQ_ORDER:
+//   out[8c + ORDER[i]][k0/8] = transpose(in[k0 + ORDER[0..7]][c])[i].
+// A thread handles eight consecutive row words (64 values of K), so each output row receives
+// a full 32-byte sector written with two 16-byte stores, while the 32 threads of a warp read
+// 32 consecutive input words (128 contiguous bytes) per load. HBM-bound: 2 * N * K / 2 bytes.
+#include "tf_common.cuh"
+
+namespace tfb {
+namespace {
+
+__constant__ int kAwqOrder[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+
+// In-register transpose of an 8x8 matrix of nibbles: element (r, j) is nibble j of w[r].
+__device__ __forceinline__ void transpose8x8_nibbles(uint32_t (&w)[8]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {  // swap 4x4 blocks: 16-bit halves of words r and r+4
+    const uint32_t a = w[r], b = w[r + 4];
+    w[r] = (a & 0x0000FFFFu) | (b << 16);
+    w[r + 4] = (a >> 16) | (b & 0xFFFF0000u);
+  }
+#pragma unroll
+  for (int base = 0; base < 8; base += 4) {  // swap 2x2 blocks: bytes of words r and r+2
+#pragma unroll
+    for (int r = base; r < base + 2; ++r) {
+      const uint32_t a = w[r], b = w[r + 2];
+      w[r] = (a & 0x00FF00FFu) | ((b << 8) & 0xFF00FF00u);
+      w[r + 2] = ((a >> 8) & 0x00FF00FFu) | (b & 0xFF00FF00u);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 8; r += 2) {  // swap single nibbles of words r and r+1
+    const uint32_t a = w[r], b = w[r + 1];
+    w[r] = (a & 0x0F0F0F0Fu) | ((b << 4) & 0xF0F0F0F0u);
+    w[r + 1] = ((a >> 4) & 0x0F0F0F0Fu) | (b & 0xF0F0F0F0u);
+  }
+}
+
+// rows = K (input rows), cols8 = N/8 (input words per row); output is [cols8*8, rows/8].
+template <bool kVecStore>
+__global__ void __launch_bounds__(128) awq_repack_kernel(const uint32_t* __restrict__ in,
+                                                         int64_t rows, int64_t cols8,
+                                                         uint32_t* __restrict__ out) {
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= cols8) return;
+  const int64_t out_words = rows / 8;                 // words per output row
+  const int64_t kw0 = static_cast<int64_t>(blockIdx.y) * 8;  // first output word column
+  const int64_t left = out_words - kw0;
+  const int nblk = left < 8 ? static_cast<int>(left) : 8;
+
+  // Two halves of four row words each: one 16-byte store per output row per half.
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t res[8][4];  // res[s][b]: output row 8c + s, word kw0 + 4h + b
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int bb = 4 * h + b;
+      if (bb < nblk) {
+        uint32_t w[8];
+        const int64_t k0 = (kw0 + bb) * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = __ldg(in + (k0 + kAwqOrder[j]) * cols8 + c);
+        transpose8x8_nibbles(w);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) res[kAwqOrder[i]][b] = w[i];
+      } else {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) res[s][b] = 0;
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      uint32_t* dst = out + (8 * c + s) * out_words + kw0 + 4 * h;
+      if (kVecStore && nblk >= 4 * h + 4) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(res[s][0], res[s][1], res[s][2], res[s][3]);
+      } else {
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          if (4 * h + b < nblk) dst[b] = res[s][b];
+      }
+    }
+  }
+}
+
+int launch_repack(const int32_t* in, int64_t rows, int64_t cols, int32_t* out,
+                  cudaStream_t stream) {
+  // rows: the packed-across dimension of the output (K for repack); cols: logical columns.
+  if (rows < 0 || cols < 0 || rows % 8 != 0 || cols % 8 != 0) return TF_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return TF_OK;
+  if (in == nullptr || out == nullptr) return TF_ERR_INVALID_ARG;
+  const int64_t cols8 = cols / 8;
+  const int64_t out_words = rows / 8;
+  const dim3 block(128);
+  const dim3 grid(static_cast<unsigned>(cdiv(cols8, 128)), static_cast<unsigned>(cdiv(out_words, 8)));
+  if (grid.y > 65535u) return TF_ERR_UNSUPPORTED;
+  const bool vec = (out_words % 4 == 0) && aligned16(out);
+  if (vec)
+    awq_repack_kernel<true><<<grid, block, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(in), rows, cols8, reinterpret_cast<uint32_t*>(out));
+  else
+    awq_repack_kernel<false><<<grid, block, 0, stream>>>(
+        reinterpret_cast<const uint32_t*>(in), rows, cols8, reinterpret_cast<uint32_t*>(out));
+  return check_launch();
+}
+
+__global__ void unpack_int4_kernel(const uint32_t* __restrict__ packed, int64_t n_words,
+                                   uint4* __restrict__ values) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= n_words) return;
+  const uint32_t v = __ldg(packed + w);
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = (v >> (4 * awq_nibble_of(j))) & 0xFu;
+  values[2 * w] = make_uint4(o[0], o[1], o[2], o[3]);
+  values[2 * w + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void pack_int4_kernel(const uint4* __restrict__ values, int64_t n_words,
+                                 uint32_t* __restrict__ packed) {
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (w >= n_words) return;
+  const uint4 a = values[2 * w], b = values[2 * w + 1];
+  const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t word = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) word |= (v[j] & 0xFu) << (4 * awq_nibble_of(j));
+  packed[w] = word;
+}
+
+}  // namespace
+}  // namespace tfb
+
+extern "C" int tf_unpack_int4(const int32_t* packed, int64_t n_words, int32_t* values,
+                              void* stream) {
+  using namespace tfb;
+  if (n_words < 0) return TF_ERR_INVALID_ARG;
+  if (n_words == 0) return TF_OK;
+  if (!packed || !values) return TF_ERR_INVALID_ARG;
+  if (!aligned16(values)) return TF_ERR_ALIGNMENT;
+  unpack_int4_kernel<<<static_cast<unsigned>(cdiv(n_words, 256)), 256, 0,
+                       static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint32_t*>(packed), n_words, reinterpret_cast<uint4*>(values));
+  return check_launch();
+}
+
+extern "C" int tf_pack_int4(const int32_t* values, int64_t n_words, int32_t* packed,
+                            void* stream) {
+  using namespace tfb;
+  if (n_words < 0) return TF_ERR_INVALID_ARG;
+  if (n_words == 0) return TF_OK;
+  if (!packed || !values) return TF_ERR_INVALID_ARG;
+  if (!aligned16(values)) return TF_ERR_ALIGNMENT;
+  pack_int4_kernel<<<static_cast<unsigned>(cdiv(n_words, 256)), 256, 0,
+                     static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(values), n_words, reinterpret_cast<uint32_t*>(packed));
+  return check_launch();
+}
+
+extern "C" int tf_awq_repack(const int32_t* qweight, int64_t K, int64_t N, int32_t* qweight_t,
+                             void* stream) {
+  return tfb::launch_repack(qweight, K, N, qweight_t, static_cast<cudaStream_t>(stream));
+}
+
+// repack_tf_to_awq (pack.py:146-148) is the same transform with the roles of K and N swapped.
+extern "C" int tf_awq_unrepack(const int32_t* qweight_t, int64_t N, int64_t K, int32_t* qweight,
+                               void* stream) {
+  return tfb::launch_repack(qweight_t, N, K, qweight, static_cast<cudaStream_t>(stream));
+}

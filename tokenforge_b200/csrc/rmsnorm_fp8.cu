@@ -1,0 +1,212 @@
+// Fused RMSNorm + FP8 e4m3 activation quantization, one pass over HBM.
+//
+// Per row (reference tokenforge/kernels/triton/rmsnorm_fp8.py:44-73; torch rule
+// tokenforge/kernels/reference.py:35-56):
+//   var   = sum(x^2) / H                        (fp32)
+//   rstd  = 1 / sqrt_rn(var + eps)              (IEEE sqrt, IEEE division)
+//   y     = fp16(x * rstd) * weight             (round to fp16, then an fp16 product)
+//   scale = max(amax|y| / 448, 1 / (448 * 512)) (dynamic, per token) or the static scale
+//   q     = e4m3_rne(clamp(y / scale, -448, 448)) with an IEEE division
+// The clamp and the cast are one hardware conversion: cvt.rn.satfinite.e4m3x2.f32 saturates
+// finite and infinite values to +-448, keeps NaN, and rounds to nearest even including the
+// subnormal range and the sign of zero (so -0.0 becomes code 0x80).
+//
+// Fast path: one warp per row with the row held in registers as fp16 (x is read from HBM once,
+// q written once): H/8 16-byte vectors spread over the 32 lanes, warp-shuffle reductions, no
+// shared memory. Generic path (any H, any alignment, H > 4096): one CTA per row, three sweeps
+// over the row (the second and third hit L2).
+#include "tf_common.cuh"
+
+namespace tfb {
+namespace {
+
+constexpr float kFp8Max = 448.0f;
+constexpr float kMinScale = 1.0f / (448.0f * 512.0f);
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float rstd_of(float sumsq, int64_t H, float eps) {
+  const float var = __fdiv_rn(sumsq, static_cast<float>(H));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+__device__ __forceinline__ float dyn_scale(float amax) {
+  return fmaxf(__fdiv_rn(amax, kFp8Max), kMinScale);
+}
+
+// VPL = 16-byte vectors per lane; rows of H <= 256 * VPL elements, H % 8 == 0, aligned.
+template <int VPL>
+__global__ void __launch_bounds__(128) rmsnorm_fp8_warp_kernel(
+    const uint4* __restrict__ x, int64_t T, int64_t H, int64_t ldx_vec,
+    const uint4* __restrict__ weight, float eps, const float* __restrict__ static_scale,
+    uint2* __restrict__ q, float* __restrict__ scale_out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int64_t nvec = H / 8;
+  const uint4* xr = x + row * ldx_vec;
+
+  uint4 v[VPL];
+  float sumsq = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int64_t j = lane + 32 * i;
+    v[i] = (j < nvec) ? ldg_stream_v4(xr + j) : make_uint4(0, 0, 0, 0);
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      sumsq = fmaf(f.x, f.x, sumsq);
+      sumsq = fmaf(f.y, f.y, sumsq);
+    }
+  }
+  const float rstd = rstd_of(warp_sum(sumsq), H, eps);
+
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int64_t j = lane + 32 * i;
+    if (j >= nvec) continue;
+    const uint4 wv = __ldg(weight + j);
+    __half2* h = reinterpret_cast<__half2*>(&v[i]);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      const __half2 n2 = __halves2half2(__float2half_rn(__fmul_rn(f.x, rstd)),
+                                        __float2half_rn(__fmul_rn(f.y, rstd)));
+      h[e] = __hmul2(n2, w2[e]);
+      const float2 y = __half22float2(h[e]);
+      amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
+    }
+  }
+  float scale;
+  if (static_scale != nullptr) {
+    scale = __ldg(static_scale);
+  } else {
+    scale = dyn_scale(warp_max(amax));
+    if (lane == 0) scale_out[row] = scale;
+  }
+  uint2* qr = q + row * nvec;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int64_t j = lane + 32 * i;
+    if (j >= nvec) continue;
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+    uint32_t packed[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float2 a = __half22float2(h[2 * e]);
+      const float2 b = __half22float2(h[2 * e + 1]);
+      const uint32_t lo = cvt_e4m3x2(__fdiv_rn(a.x, scale), __fdiv_rn(a.y, scale));
+      const uint32_t hi = cvt_e4m3x2(__fdiv_rn(b.x, scale), __fdiv_rn(b.y, scale));
+      packed[e] = lo | (hi << 16);
+    }
+    qr[j] = make_uint2(packed[0], packed[1]);
+  }
+}
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
+  v = is_max ? warp_max(v) : warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float r = is_max ? 0.f : 0.f;
+  for (int w = 0; w < nw; ++w) r = is_max ? fmaxf(r, sh[w]) : r + sh[w];
+  return r;
+}
+
+__device__ __forceinline__ __half norm_elem(const __half* xr, const __half* w, int64_t i,
+                                            float rstd) {
+  const float f = __half2float(xr[i]);
+  return __hmul(__float2half_rn(__fmul_rn(f, rstd)), w[i]);
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_fp8_generic_kernel(
+    const __half* __restrict__ x, int64_t T, int64_t H, int64_t ldx,
+    const __half* __restrict__ weight, float eps, const float* __restrict__ static_scale,
+    uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  __shared__ float sh[32];
+  const int64_t row = blockIdx.x;
+  const __half* xr = x + row * ldx;
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+    const float f = __half2float(xr[i]);
+    s = fmaf(f, f, s);
+  }
+  const float rstd = rstd_of(block_reduce(s, false, sh), H, eps);
+  float scale;
+  if (static_scale != nullptr) {
+    scale = *static_scale;
+  } else {
+    float amax = 0.f;
+    for (int64_t i = threadIdx.x; i < H; i += blockDim.x)
+      amax = fmaxf(amax, fabsf(__half2float(norm_elem(xr, weight, i, rstd))));
+    scale = dyn_scale(block_reduce(amax, true, sh));
+    if (threadIdx.x == 0) scale_out[row] = scale;
+  }
+  for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+    const float y = __half2float(norm_elem(xr, weight, i, rstd));
+    q[row * H + i] = static_cast<uint8_t>(cvt_e4m3x2(__fdiv_rn(y, scale), 0.f) & 0xFFu);
+  }
+}
+
+__global__ void cast_e4m3_kernel(const float* __restrict__ in, int64_t n, uint8_t* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = static_cast<uint8_t>(cvt_e4m3x2(in[i], 0.f) & 0xFFu);
+}
+
+}  // namespace
+}  // namespace tfb
+
+extern "C" int tf_rmsnorm_fp8_quant(const uint16_t* x, int64_t T, int64_t H, int64_t ldx,
+                                    const uint16_t* weight, float eps, const float* static_scale,
+                                    uint8_t* q, float* scale_out, void* stream_) {
+  using namespace tfb;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (T < 0 || H <= 0 || ldx < H) return TF_ERR_INVALID_ARG;
+  if (T == 0) return TF_OK;
+  if (!x || !weight || !q || (!static_scale && !scale_out)) return TF_ERR_INVALID_ARG;
+  const bool vec_ok = (H % 8 == 0) && (ldx % 8 == 0) && aligned16(x) && aligned16(weight) &&
+                      (reinterpret_cast<uintptr_t>(q) % 8 == 0);
+  const int64_t nvec = H / 8;
+  const int rows_per_cta = 4;
+  const unsigned grid = static_cast<unsigned>(cdiv(T, rows_per_cta));
+  auto xv = reinterpret_cast<const uint4*>(x);
+  auto wv = reinterpret_cast<const uint4*>(weight);
+  auto qv = reinterpret_cast<uint2*>(q);
+  if (vec_ok && nvec <= 32 * 4) {
+    rmsnorm_fp8_warp_kernel<4><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
+  } else if (vec_ok && nvec <= 32 * 8) {
+    rmsnorm_fp8_warp_kernel<8><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
+  } else if (vec_ok && nvec <= 32 * 16) {
+    rmsnorm_fp8_warp_kernel<16><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
+  } else {
+    if (T > 0x7fffffffLL) return TF_ERR_UNSUPPORTED;
+    rmsnorm_fp8_generic_kernel<<<static_cast<unsigned>(T), 256, 0, stream>>>(
+        reinterpret_cast<const __half*>(x), T, H, ldx, reinterpret_cast<const __half*>(weight),
+        eps, static_scale, q, scale_out);
+  }
+  return check_launch();
+}
+
+extern "C" int tf_cast_e4m3(const float* in, int64_t n, uint8_t* out, void* stream) {
+  using namespace tfb;
+  if (n < 0) return TF_ERR_INVALID_ARG;
+  if (n == 0) return TF_OK;
+  if (!in || !out) return TF_ERR_INVALID_ARG;
+  cast_e4m3_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0,
+                     static_cast<cudaStream_t>(stream)>>>(in, n, out);
+  return check_launch();
+}

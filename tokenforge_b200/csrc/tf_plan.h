@@ -1,0 +1,53 @@
+// Host-side launch plan shared by the C ABI and the kernels' launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace tfb {
+
+enum LinearKernel : int {
+  kKernelGemv = 0,     // warp-level MMA, one 8-token tile (M <= 8)
+  kKernelMmaGemm = 1,  // warp-level MMA, 64-token tiles
+  kKernelTcGemm = 2,   // tcgen05 + TMEM + TMA tensor-core GEMM
+};
+
+struct LinearPlan {
+  int kernel;
+  int m_bucket;          // smallest launch-table bucket >= M
+  int tile_n;            // weight rows per warp tile (mma) or per CTA tile (tcgen05)
+  int warps_k;           // warps splitting K inside one CTA (mma kernels)
+  int split_k;           // CTAs splitting K (partials reduced in a fixed order)
+  int tile_m;            // tokens per CTA tile
+  int blocks_per_split;  // 128-wide K blocks per split (mma kernels)
+  unsigned grid_x, grid_y, grid_z;
+  size_t workspace;      // bytes of scratch the launch needs
+};
+
+// Fills `plan` for y[M, N] = x[M, K] * W[N, K]^T. Returns TF_OK or an error status.
+int plan_linear(int64_t M, int64_t N, int64_t K, int group_size, LinearPlan* plan);
+
+// Process-wide launch flags (tf_set_launch_flags).
+uint32_t launch_flags();
+
+struct LinearArgs {
+  const uint16_t* x;
+  int64_t M, K, ldx;
+  const int32_t* qw;
+  const uint16_t* scales;
+  const int32_t* qzeros;
+  const uint16_t* bias;
+  int64_t N;
+  int group_size;
+  uint16_t* y;
+  int64_t ldy;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size);
+
+}  // namespace tfb

@@ -1,0 +1,363 @@
+"""``torch.ops.tokenforge.*`` custom ops backed by the sm_100a kernel library.
+
+Same op names, schemas, fake implementations and error messages as the reference's
+tokenforge/kernels/ops.py (ADR 0004: custom ops with fakes, no host syncs, no host reads of
+tensor values, shape-only dispatch), plus ``tokenforge::awq_repack``:
+
+* ``tokenforge::w4a16_linear(x, qweight_t, scales, qzeros, bias, group_size, backend) -> y``
+* ``tokenforge::w4a16_dequant(qweight_t, scales, qzeros, group_size) -> w [N, K] fp16``
+* ``tokenforge::rmsnorm_fp8_quant(x, weight, eps, scale) -> (q e4m3, scale fp32)``
+* ``tokenforge::awq_repack(qweight) -> qweight_t``
+
+Every real implementation enqueues kernels on the current CUDA stream through the C ABI; the
+only allocations are outputs and the optional split-K workspace, both from PyTorch's caching
+allocator. CPU tensors raise: there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import functools
+
+import torch
+
+from tokenforge_b200 import _lib, dispatch
+from tokenforge_b200.pack import PACK_FACTOR
+
+_VEC = 16  # bytes: alignment the vectorised kernels require
+
+
+def cuda_ext_available() -> bool:
+    """The kernel library is built and loadable."""
+    return _ext() is not None
+
+
+@functools.cache
+def _ext():  # type: ignore[no-untyped-def]
+    try:
+        return _lib.lib()
+    except (ImportError, OSError):
+        return None
+
+
+def _require(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (tokenforge_b200 has no CPU path)")
+
+
+def _aligned_rows(x2: torch.Tensor) -> torch.Tensor:
+    """x2 with unit stride along K, a 16-byte aligned base and a row stride multiple of 8."""
+    if x2.stride(-1) != 1 or x2.data_ptr() % _VEC != 0 or (x2.shape[0] > 1 and x2.stride(0) % 8):
+        x2 = x2.clone(memory_format=torch.contiguous_format)
+    return x2
+
+
+def _check_inputs(
+    x: torch.Tensor,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    group_size: int,
+) -> tuple[int, int, int]:
+    """Shape/dtype/layout contract of the reference (triton/w4a16.py:149-175)."""
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D [M, K], got shape {tuple(x.shape)}")
+    if x.dtype != torch.float16:
+        raise TypeError(f"x must be fp16, got {x.dtype}")
+    m, k = x.shape
+    n = qweight_t.shape[0]
+    if qweight_t.dtype != torch.int32 or qzeros.dtype != torch.int32:
+        raise TypeError("qweight_t and qzeros must be int32")
+    if scales.dtype != torch.float16:
+        raise TypeError(f"scales must be fp16, got {scales.dtype}")
+    if qweight_t.shape[1] * PACK_FACTOR != k:
+        raise ValueError(f"x has K={k} but qweight_t encodes K={qweight_t.shape[1] * PACK_FACTOR}")
+    if group_size not in (32, 64, 128):
+        raise ValueError(f"group_size {group_size} must be 32, 64 or 128 and divide K")
+    if k % group_size != 0:
+        raise ValueError(f"K={k} is not a multiple of group_size={group_size}")
+    if n % PACK_FACTOR != 0:
+        raise ValueError(f"N={n} is not a multiple of {PACK_FACTOR}")
+    if tuple(scales.shape) != (k // group_size, n):
+        raise ValueError(f"scales shape {tuple(scales.shape)} != {(k // group_size, n)}")
+    if tuple(qzeros.shape) != (k // group_size, n // PACK_FACTOR):
+        raise ValueError(
+            f"qzeros shape {tuple(qzeros.shape)} != {(k // group_size, n // PACK_FACTOR)}"
+        )
+    for name, t in (("qweight_t", qweight_t), ("scales", scales), ("qzeros", qzeros)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if x.stride(1) != 1:
+        raise ValueError("x must be contiguous along K (stride(1) == 1)")
+    return m, n, k
+
+
+_LINEAR_ENTRY = {"linear": "tf_w4a16_linear", "gemv": "tf_w4a16_gemv", "gemm": "tf_w4a16_gemm"}
+
+
+def _launch_linear(
+    entry: str,
+    x2: torch.Tensor,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    bias: torch.Tensor | None,
+    group_size: int,
+) -> torch.Tensor:
+    m, n, k = _check_inputs(x2, qweight_t, scales, qzeros, group_size)
+    for name, t in (("x", x2), ("qweight_t", qweight_t), ("scales", scales), ("qzeros", qzeros)):
+        _require(t, name)
+    if bias is not None:
+        _require(bias, "bias")
+        if tuple(bias.shape) != (n,):
+            raise ValueError(f"bias shape {tuple(bias.shape)} != {(n,)}")
+        if bias.dtype != torch.float16:
+            raise TypeError(f"bias must be fp16, got {bias.dtype}")
+        bias = bias.contiguous()
+    y = torch.empty((m, n), dtype=torch.float16, device=x2.device)
+    if m == 0:
+        return y
+    x2 = _aligned_rows(x2)
+    lib = _lib.lib()
+    ws_bytes = int(lib.tf_w4a16_workspace_bytes(m, n, k, group_size))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x2.device) if ws_bytes else None
+    with torch.cuda.device(x2.device):
+        status = getattr(lib, _LINEAR_ENTRY[entry])(
+            x2.data_ptr(), m, k, x2.stride(0),
+            qweight_t.data_ptr(), scales.data_ptr(), qzeros.data_ptr(), _lib.ptr(bias),
+            n, group_size, y.data_ptr(), n, _lib.ptr(ws), ws_bytes, _lib.stream_ptr(x2.device),
+        )  # fmt: skip
+    _lib.check(_LINEAR_ENTRY[entry], status)
+    return y
+
+
+def w4a16_gemm(
+    x: torch.Tensor,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    group_size: int,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``x [M, K] fp16 @ dequant(W)^T (+ bias) -> [M, N] fp16`` through the launch table."""
+    return _launch_linear("linear", x, qweight_t, scales, qzeros, bias, group_size)
+
+
+def w4a16_gemv(x, qweight_t, scales, qzeros, bias, group_size):  # type: ignore[no-untyped-def]
+    """Decode entry (M <= 8): the ``_C.w4a16_gemv`` contract of the reference (ops.py:86-88)."""
+    return _launch_linear("gemv", x, qweight_t, scales, qzeros, bias, group_size)
+
+
+def w4a16_gemm_tc(x, qweight_t, scales, qzeros, bias, group_size):  # type: ignore[no-untyped-def]
+    """Prefill entry: the tensor-core GEMM for any M (used by tests to pin each kernel)."""
+    return _launch_linear("gemm", x, qweight_t, scales, qzeros, bias, group_size)
+
+
+@torch.library.custom_op("tokenforge::w4a16_linear", mutates_args=())
+def w4a16_linear(
+    x: torch.Tensor,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    bias: torch.Tensor | None,
+    group_size: int,
+    backend: str,
+) -> torch.Tensor:
+    k = x.shape[-1]
+    n = qweight_t.shape[0]
+    out_shape = (*x.shape[:-1], n)
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    if m == 0:
+        return x.new_empty(out_shape)
+    if backend not in ("triton", "cuda"):
+        raise ValueError(f"backend must be 'triton' or 'cuda' at op level, got {backend!r}")
+    decision = dispatch.select(
+        m, backend=backend, on_gpu=x.is_cuda, cuda_ext_available=cuda_ext_available()  # type: ignore[arg-type]
+    )
+    dispatch.record(decision)
+    entry = "gemv" if decision.kernel == "cuda_gemv" else "gemm"
+    return _launch_linear(entry, x2, qweight_t, scales, qzeros, bias, group_size).reshape(out_shape)
+
+
+@w4a16_linear.register_fake
+def _w4a16_linear_fake(x, qweight_t, scales, qzeros, bias, group_size, backend):  # type: ignore[no-untyped-def]
+    return x.new_empty((*x.shape[:-1], qweight_t.shape[0]))
+
+
+@torch.library.custom_op("tokenforge::w4a16_dequant", mutates_args=())
+def w4a16_dequant(
+    qweight_t: torch.Tensor, scales: torch.Tensor, qzeros: torch.Tensor, group_size: int
+) -> torch.Tensor:
+    for name, t in (("qweight_t", qweight_t), ("scales", scales), ("qzeros", qzeros)):
+        _require(t, name)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    n, k = qweight_t.shape[0], qweight_t.shape[1] * PACK_FACTOR
+    if group_size not in (32, 64, 128) or k % group_size:
+        raise ValueError(f"K={k} is not a multiple of group_size={group_size}")
+    if tuple(scales.shape) != (k // group_size, n) or tuple(qzeros.shape) != (
+        k // group_size,
+        n // PACK_FACTOR,
+    ):
+        raise ValueError("scales/qzeros shape does not match qweight_t")
+    out = torch.empty((n, k), dtype=torch.float16, device=qweight_t.device)
+    with torch.cuda.device(qweight_t.device):
+        status = _lib.lib().tf_w4a16_dequant(
+            qweight_t.data_ptr(), scales.data_ptr(), qzeros.data_ptr(), n, k, group_size,
+            out.data_ptr(), _lib.stream_ptr(qweight_t.device),
+        )  # fmt: skip
+    _lib.check("tf_w4a16_dequant", status)
+    return out
+
+
+@w4a16_dequant.register_fake
+def _w4a16_dequant_fake(qweight_t, scales, qzeros, group_size):  # type: ignore[no-untyped-def]
+    return qweight_t.new_empty((qweight_t.shape[0], qweight_t.shape[1] * 8), dtype=torch.float16)
+
+
+def rmsnorm_fp8_quant_2d(
+    x: torch.Tensor, weight: torch.Tensor, eps: float, scale: torch.Tensor | None = None
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``x [T, H]`` -> ``(q [T, H] e4m3, scale)``; contract of triton/rmsnorm_fp8.py:76-117.
+
+    ``scale`` is ``[T, 1]`` fp32 (dynamic per token) or the given single-element fp32 tensor
+    (static per tensor), which is returned as is.
+    """
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D [T, H], got {tuple(x.shape)}")
+    t, h = x.shape
+    if tuple(weight.shape) != (h,):
+        raise ValueError(f"weight shape {tuple(weight.shape)} != {(h,)}")
+    if x.stride(1) != 1:
+        raise ValueError("x must be contiguous along H")
+    if x.dtype != torch.float16 or weight.dtype != torch.float16:
+        raise TypeError("x and weight must be fp16")
+    if scale is not None and (scale.numel() != 1 or scale.dtype != torch.float32):
+        raise ValueError("static scale must be a single fp32 element")
+    _require(x, "x")
+    _require(weight, "weight")
+    out = torch.empty((t, h), dtype=torch.float8_e4m3fn, device=x.device)
+    scale_out = torch.empty((t, 1), dtype=torch.float32, device=x.device) if scale is None else scale
+    if t == 0:
+        return out, scale_out
+    if scale is not None:
+        _require(scale, "scale")
+    if x.data_ptr() % _VEC or (t > 1 and x.stride(0) % 8):
+        x = x.clone(memory_format=torch.contiguous_format)
+    weight = weight.contiguous()
+    with torch.cuda.device(x.device):
+        status = _lib.lib().tf_rmsnorm_fp8_quant(
+            x.data_ptr(), t, h, x.stride(0) if t > 1 else h, weight.data_ptr(), float(eps),
+            _lib.ptr(scale), out.data_ptr(), None if scale is not None else scale_out.data_ptr(),
+            _lib.stream_ptr(x.device),
+        )  # fmt: skip
+    _lib.check("tf_rmsnorm_fp8_quant", status)
+    return out, scale_out
+
+
+@torch.library.custom_op("tokenforge::rmsnorm_fp8_quant", mutates_args=())
+def rmsnorm_fp8_quant(
+    x: torch.Tensor, weight: torch.Tensor, eps: float, scale: torch.Tensor | None
+) -> tuple[torch.Tensor, torch.Tensor]:
+    h = x.shape[-1]
+    x2 = x.reshape(-1, h)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    q, s = rmsnorm_fp8_quant_2d(x2, weight, eps, scale)
+    if scale is not None:
+        s = s.clone()  # a custom op may not return an alias of an input
+    return q.reshape(x.shape), s.reshape((*x.shape[:-1], 1)) if scale is None else s
+
+
+@rmsnorm_fp8_quant.register_fake
+def _rmsnorm_fp8_quant_fake(x, weight, eps, scale):  # type: ignore[no-untyped-def]
+    q = x.new_empty(x.shape, dtype=torch.float8_e4m3fn)
+    if scale is None:
+        return q, x.new_empty((*x.shape[:-1], 1), dtype=torch.float32)
+    return q, torch.empty_like(scale)
+
+
+def _check_packed(t: torch.Tensor, name: str) -> None:
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if t.dtype != torch.int32:
+        raise TypeError(f"{name} must be int32, got {t.dtype}")
+    _require(t, name)
+
+
+@torch.library.custom_op("tokenforge::awq_repack", mutates_args=())
+def awq_repack(qweight: torch.Tensor) -> torch.Tensor:
+    """AWQ ``qweight [K, N/8]`` -> ``qweight_t [N, K/8]``, bit-exact with repack_awq_to_tf."""
+    _check_packed(qweight, "qweight")
+    k, n8 = qweight.shape
+    if k % PACK_FACTOR:
+        raise ValueError(f"K={k} is not a multiple of {PACK_FACTOR}")
+    qweight = qweight.contiguous()
+    out = torch.empty((n8 * PACK_FACTOR, k // PACK_FACTOR), dtype=torch.int32, device=qweight.device)
+    with torch.cuda.device(qweight.device):
+        status = _lib.lib().tf_awq_repack(
+            qweight.data_ptr(), k, n8 * PACK_FACTOR, out.data_ptr(), _lib.stream_ptr(qweight.device)
+        )
+    _lib.check("tf_awq_repack", status)
+    return out
+
+
+@awq_repack.register_fake
+def _awq_repack_fake(qweight):  # type: ignore[no-untyped-def]
+    return qweight.new_empty((qweight.shape[1] * 8, qweight.shape[0] // 8))
+
+
+def awq_unrepack_cuda(qweight_t: torch.Tensor) -> torch.Tensor:
+    """Kernel ``qweight_t [N, K/8]`` -> AWQ ``qweight [K, N/8]`` (repack_tf_to_awq)."""
+    _check_packed(qweight_t, "qweight_t")
+    n, k8 = qweight_t.shape
+    if n % PACK_FACTOR:
+        raise ValueError(f"N={n} is not a multiple of {PACK_FACTOR}")
+    qweight_t = qweight_t.contiguous()
+    out = torch.empty((k8 * PACK_FACTOR, n // PACK_FACTOR), dtype=torch.int32, device=qweight_t.device)
+    with torch.cuda.device(qweight_t.device):
+        status = _lib.lib().tf_awq_unrepack(
+            qweight_t.data_ptr(), n, k8 * PACK_FACTOR, out.data_ptr(),
+            _lib.stream_ptr(qweight_t.device),
+        )  # fmt: skip
+    _lib.check("tf_awq_unrepack", status)
+    return out
+
+
+def unpack_int4_cuda(packed: torch.Tensor) -> torch.Tensor:
+    _require(packed, "packed")
+    p = packed.contiguous()
+    out = torch.empty((*p.shape[:-1], p.shape[-1] * PACK_FACTOR), dtype=torch.int32, device=p.device)
+    with torch.cuda.device(p.device):
+        status = _lib.lib().tf_unpack_int4(
+            p.data_ptr(), p.numel(), out.data_ptr(), _lib.stream_ptr(p.device)
+        )
+    _lib.check("tf_unpack_int4", status)
+    return out
+
+
+def pack_int4_cuda(values: torch.Tensor) -> torch.Tensor:
+    _require(values, "values")
+    v = values.to(torch.int32).contiguous()
+    if v.data_ptr() % _VEC:
+        v = v.clone()
+    out = torch.empty((*v.shape[:-1], v.shape[-1] // PACK_FACTOR), dtype=torch.int32, device=v.device)
+    with torch.cuda.device(v.device):
+        status = _lib.lib().tf_pack_int4(
+            v.data_ptr(), out.numel(), out.data_ptr(), _lib.stream_ptr(v.device)
+        )
+    _lib.check("tf_pack_int4", status)
+    return out
+
+
+def cast_e4m3(values: torch.Tensor) -> torch.Tensor:
+    """fp32 -> e4m3 with the quantizer's rounding (RNE, saturating, NaN kept)."""
+    _require(values, "values")
+    v = values.to(torch.float32).contiguous()
+    out = torch.empty(v.shape, dtype=torch.float8_e4m3fn, device=v.device)
+    with torch.cuda.device(v.device):
+        status = _lib.lib().tf_cast_e4m3(v.data_ptr(), v.numel(), out.data_ptr(), _lib.stream_ptr(v.device))
+    _lib.check("tf_cast_e4m3", status)
+    return out
