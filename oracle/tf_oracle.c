@@ -163,7 +163,8 @@ uint8_t oracle_e4m3(float v) {
 }
 
 /* RMSNorm + e4m3 quantization (reference.py:35-56 for the rule; triton/rmsnorm_fp8.py:57-73
- * for the exact fp32 operations: IEEE sqrt and divisions). The sum of squares runs in H order.
+ * for the exact fp32 operations: IEEE sqrt and divisions). The sum of squares is accumulated
+ * in fp64 and rounded once to fp32, so it does not depend on the summation order.
  * scale_out[t] receives the dynamic per-token scale when static_scale is NULL. */
 void oracle_rmsnorm_fp8(const uint16_t* x, int64_t T, int64_t H, const uint16_t* weight,
                         float eps, const float* static_scale, uint8_t* q, float* scale_out) {
@@ -171,12 +172,14 @@ void oracle_rmsnorm_fp8(const uint16_t* x, int64_t T, int64_t H, const uint16_t*
 #pragma omp parallel for schedule(static)
   for (int64_t t = 0; t < T; ++t) {
     const uint16_t* xr = x + t * H;
-    float ss = 0.0f;
+    /* fp16 squares are exact in fp32; their fp64 sum rounded once to fp32 is the sum of
+     * squares independent of summation order (the CUDA kernel accumulates the same way). */
+    double ss = 0.0;
     for (int64_t i = 0; i < H; ++i) {
       const float f = (float)h_from_bits(xr[i]);
-      ss += f * f;
+      ss += (double)(f * f);
     }
-    const float var = ss / (float)H;
+    const float var = (float)ss / (float)H;
     const float rstd = 1.0f / sqrtf(var + eps);
     float amax = 0.0f;
     for (int64_t i = 0; i < H; ++i) {

@@ -2,7 +2,7 @@
 //
 // Per row (reference tokenforge/kernels/triton/rmsnorm_fp8.py:44-73; torch rule
 // tokenforge/kernels/reference.py:35-56):
-//   var   = sum(x^2) / H                        (fp32)
+//   var   = fp32(sum(x^2)) / H                  (sum accumulated in fp64, then fp32)
 //   rstd  = 1 / sqrt_rn(var + eps)              (IEEE sqrt, IEEE division)
 //   y     = fp16(x * rstd) * weight             (round to fp16, then an fp16 product)
 //   scale = max(amax|y| / 448, 1 / (448 * 512)) (dynamic, per token) or the static scale
@@ -23,7 +23,7 @@ namespace {
 constexpr float kFp8Max = 448.0f;
 constexpr float kMinScale = 1.0f / (448.0f * 512.0f);
 
-__device__ __forceinline__ float warp_sum(float v) {
+__device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
@@ -34,8 +34,11 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__device__ __forceinline__ float rstd_of(float sumsq, int64_t H, float eps) {
-  const float var = __fdiv_rn(sumsq, static_cast<float>(H));
+// The sum of squares is accumulated in fp64: every fp16 square is exact in fp32 and the fp64 sum
+// of up to ~1e6 of them is exact or within 2^-53, so its fp32 rounding does not depend on the
+// summation order (threads, warps, the CPU oracle all obtain the same fp32 sum).
+__device__ __forceinline__ float rstd_of(double sumsq, int64_t H, float eps) {
+  const float var = __fdiv_rn(__double2float_rn(sumsq), static_cast<float>(H));
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 }
 
@@ -56,7 +59,7 @@ __global__ void __launch_bounds__(128) rmsnorm_fp8_warp_kernel(
   const uint4* xr = x + row * ldx_vec;
 
   uint4 v[VPL];
-  float sumsq = 0.f;
+  double sumsq = 0.0;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int64_t j = lane + 32 * i;
@@ -65,8 +68,7 @@ __global__ void __launch_bounds__(128) rmsnorm_fp8_warp_kernel(
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 f = __half22float2(h[e]);
-      sumsq = fmaf(f.x, f.x, sumsq);
-      sumsq = fmaf(f.y, f.y, sumsq);
+      sumsq += static_cast<double>(__fmul_rn(f.x, f.x)) + static_cast<double>(__fmul_rn(f.y, f.y));
     }
   }
   const float rstd = rstd_of(warp_sum(sumsq), H, eps);
@@ -115,15 +117,25 @@ __global__ void __launch_bounds__(128) rmsnorm_fp8_warp_kernel(
   }
 }
 
-__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
-  v = is_max ? warp_max(v) : warp_sum(v);
+__device__ __forceinline__ float block_max(float v, float* sh) {
+  v = warp_max(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __syncthreads();
   if (lane == 0) sh[warp] = v;
   __syncthreads();
-  const int nw = blockDim.x >> 5;
-  float r = is_max ? 0.f : 0.f;
-  for (int w = 0; w < nw; ++w) r = is_max ? fmaxf(r, sh[w]) : r + sh[w];
+  float r = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) r = fmaxf(r, sh[w]);
+  return r;
+}
+
+__device__ __forceinline__ double block_sum(double v, double* sh) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  double r = 0.0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) r += sh[w];
   return r;
 }
 
@@ -138,14 +150,15 @@ __global__ void __launch_bounds__(256) rmsnorm_fp8_generic_kernel(
     const __half* __restrict__ weight, float eps, const float* __restrict__ static_scale,
     uint8_t* __restrict__ q, float* __restrict__ scale_out) {
   __shared__ float sh[32];
+  __shared__ double shd[32];
   const int64_t row = blockIdx.x;
   const __half* xr = x + row * ldx;
-  float s = 0.f;
+  double s = 0.0;
   for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
     const float f = __half2float(xr[i]);
-    s = fmaf(f, f, s);
+    s += static_cast<double>(__fmul_rn(f, f));
   }
-  const float rstd = rstd_of(block_reduce(s, false, sh), H, eps);
+  const float rstd = rstd_of(block_sum(s, shd), H, eps);
   float scale;
   if (static_scale != nullptr) {
     scale = *static_scale;
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fp8_generic_kernel(
     float amax = 0.f;
     for (int64_t i = threadIdx.x; i < H; i += blockDim.x)
       amax = fmaxf(amax, fabsf(__half2float(norm_elem(xr, weight, i, rstd))));
-    scale = dyn_scale(block_reduce(amax, true, sh));
+    scale = dyn_scale(block_max(amax, sh));
     if (threadIdx.x == 0) scale_out[row] = scale;
   }
   for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
