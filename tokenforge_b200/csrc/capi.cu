@@ -88,14 +88,7 @@ int plan_linear(int64_t M, int64_t N, int64_t K, int group_size, LinearPlan* pl)
     pl->kernel = kKernelMmaGemm;
   if (pl->kernel == kKernelTcGemm) {
     pl->tile_m = kTable[idx].tile_m;
-    pl->tile_n = 128;
-    pl->warps_k = 1;
-    pl->split_k = 1;
-    pl->blocks_per_split = 0;
-    pl->grid_x = static_cast<unsigned>(cdiv(N, 128));
-    pl->grid_y = 1;
-    pl->grid_z = static_cast<unsigned>(cdiv(M, pl->tile_m));
-    pl->workspace = 0;
+    plan_tc(M, N, K, pl);
     return TF_OK;
   }
   return plan_mma(M, N, K, pl);
@@ -131,11 +124,7 @@ int run_linear(const LinearArgs& a, cudaStream_t stream, int force_kernel) {
     } else {
       pl.kernel = kKernelTcGemm;
       pl.tile_m = 16;
-      pl.tile_n = 128;
-      pl.grid_x = static_cast<unsigned>(cdiv(a.N, 128));
-      pl.grid_y = 1;
-      pl.grid_z = static_cast<unsigned>(cdiv(a.M, 16));
-      pl.workspace = 0;
+      plan_tc(a.M, a.N, a.K, &pl);
     }
   }
   if (pl.workspace > 0 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace))

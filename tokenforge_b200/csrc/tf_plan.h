@@ -49,5 +49,10 @@ struct LinearArgs {
 int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size);
+// Fills split_k / blocks_per_split / grid / workspace of a tensor-core plan whose tile_m is set.
+void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* plan);
+// y[m, n] = fp16(sum_s partial[s, m, n] + bias[n]), splits summed in order 0..split-1.
+int launch_splitk_reduce(const float* partial, int split, int64_t M, int64_t N,
+                         const uint16_t* bias, uint16_t* y, int64_t ldy, cudaStream_t stream);
 
 }  // namespace tfb

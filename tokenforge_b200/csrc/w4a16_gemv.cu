@@ -47,30 +47,74 @@ struct MmaParams {
   int blocks_per_split;
 };
 
-constexpr int kUnroll = 2;  // K blocks per pipeline stage per warp (two stages in registers)
-
+// One K block (128 values of k) of one warp tile, as held in registers between the moment its
+// loads are issued and the moment it is consumed.
 template <int MT>
-__device__ __forceinline__ void mma_block(float (&acc)[MT][4], const uint4& wa, const uint4& wb,
-                                          bool kv, int64_t k, const MmaParams& p, int64_t rowA,
-                                          int64_t rowB, bool okA, bool okB, int64_t m_base,
-                                          int q) {
-  __half2 zzA = zero_magic2(0), zzB = zero_magic2(0);
-  __half2 ssA = __float2half2_rn(0.f), ssB = __float2half2_rn(0.f);
-  if (kv) {
-    const int64_t g = k / p.group_size;
-    if (okA) {
-      const __half s = __ldg(p.scales + g * p.N + rowA);
-      ssA = __halves2half2(s, s);
-      zzA = zero_magic2(zero_of(p.qzeros + g * (p.N / 8), rowA));
+struct Slot {
+  uint4 wa, wb;                 // packed weights of rows A = n0+q and B = n0+q+8 (16 B each)
+  __half sa, sb;                // scales of the block's group for rows A and B
+  uint32_t za, zb;              // qzeros words holding the rows' zero points
+  uint4 x[MT == 1 ? 4 : 1];     // activations x[q][k..k+31] (decode tile only)
+  int64_t k;                    // first k of this lane's 32-value chunk
+  bool kv;                      // the block exists (k < K and inside this CTA's K range)
+};
+
+struct TileGeom {
+  int64_t rowA, rowB, m_base;
+  bool okA, okB;
+  int q, c, b_end;
+  const int32_t* wA;
+  const int32_t* wB;
+};
+
+// Weights, scales and zero points: never written by the preceding kernel, so these loads may be
+// issued before the programmatic-dependent-launch wait.
+template <int MT>
+__device__ __forceinline__ void load_weights(Slot<MT>& s, int bb, const MmaParams& p,
+                                             const TileGeom& t) {
+  s.k = static_cast<int64_t>(bb) * 128 + 32 * t.c;
+  s.kv = bb < t.b_end && s.k < p.K;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  s.wa = (s.kv && t.okA) ? ldg_stream_v4(t.wA + static_cast<int64_t>(bb) * 16) : zero;
+  s.wb = (s.kv && t.okB) ? ldg_stream_v4(t.wB + static_cast<int64_t>(bb) * 16) : zero;
+  s.sa = s.sb = __ushort_as_half(0);
+  s.za = s.zb = 0;
+  if (s.kv) {
+    const int64_t g = s.k / p.group_size;
+    if (t.okA) {
+      s.sa = __ldg(p.scales + g * p.N + t.rowA);
+      s.za = static_cast<uint32_t>(__ldg(p.qzeros + g * (p.N / 8) + (t.rowA >> 3)));
     }
-    if (okB) {
-      const __half s = __ldg(p.scales + g * p.N + rowB);
-      ssB = __halves2half2(s, s);
-      zzB = zero_magic2(zero_of(p.qzeros + g * (p.N / 8), rowB));
+    if (t.okB) {
+      s.sb = __ldg(p.scales + g * p.N + t.rowB);
+      s.zb = static_cast<uint32_t>(__ldg(p.qzeros + g * (p.N / 8) + (t.rowB >> 3)));
     }
   }
-  const uint32_t wa_w[4] = {wa.x, wa.y, wa.z, wa.w};
-  const uint32_t wb_w[4] = {wb.x, wb.y, wb.z, wb.w};
+}
+
+// Activations (decode tile only; the 64-token tile reads them while computing).
+template <int MT>
+__device__ __forceinline__ void load_acts(Slot<MT>& s, const MmaParams& p, const TileGeom& t) {
+  if constexpr (MT == 1) {
+    const int64_t m = t.m_base + t.q;
+    const bool ok = s.kv && m < p.M;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      s.x[i] = ok ? ldg_v4(p.x + m * p.ldx + s.k + 8 * i) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int MT>
+__device__ __forceinline__ void mma_slot(float (&acc)[MT][4], const Slot<MT>& s,
+                                         const MmaParams& p, const TileGeom& t) {
+  const int nibA = 4 * awq_nibble_of(static_cast<int>(t.rowA & 7));
+  const int nibB = 4 * awq_nibble_of(static_cast<int>(t.rowB & 7));
+  const __half2 zzA = zero_magic2((s.za >> nibA) & 0xFu);
+  const __half2 zzB = zero_magic2((s.zb >> nibB) & 0xFu);
+  const __half2 ssA = __halves2half2(s.sa, s.sa);
+  const __half2 ssB = __halves2half2(s.sb, s.sb);
+  const uint32_t wa_w[4] = {s.wa.x, s.wa.y, s.wa.z, s.wa.w};
+  const uint32_t wb_w[4] = {s.wb.x, s.wb.y, s.wb.z, s.wb.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t a0[4] = {dequant_pair(magic_pair(wa_w[i], 0), zzA, ssA),
@@ -81,13 +125,18 @@ __device__ __forceinline__ void mma_block(float (&acc)[MT][4], const uint4& wa, 
                             dequant_pair(magic_pair(wb_w[i], 2), zzB, ssB),
                             dequant_pair(magic_pair(wa_w[i], 3), zzA, ssA),
                             dequant_pair(magic_pair(wb_w[i], 3), zzB, ssB)};
+    if constexpr (MT == 1) {
+      mma_16816(acc[0], a0, s.x[i].x, s.x[i].y);
+      mma_16816(acc[0], a1, s.x[i].z, s.x[i].w);
+    } else {
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const int64_t m = m_base + mt * 8 + q;
-      uint4 xv = make_uint4(0, 0, 0, 0);
-      if (kv && m < p.M) xv = ldg_v4(p.x + m * p.ldx + k + 8 * i);
-      mma_16816(acc[mt], a0, xv.x, xv.y);
-      mma_16816(acc[mt], a1, xv.z, xv.w);
+      for (int mt = 0; mt < MT; ++mt) {
+        const int64_t m = t.m_base + mt * 8 + t.q;
+        uint4 xv = make_uint4(0, 0, 0, 0);
+        if (s.kv && m < p.M) xv = ldg_v4(p.x + m * p.ldx + s.k + 8 * i);
+        mma_16816(acc[mt], a0, xv.x, xv.y);
+        mma_16816(acc[mt], a1, xv.z, xv.w);
+      }
     }
   }
 }
@@ -95,22 +144,25 @@ __device__ __forceinline__ void mma_block(float (&acc)[MT][4], const uint4& wa, 
 template <int MT, int WARPS_N, int WARPS_K>
 __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K)
     w4a16_mma_kernel(const MmaParams p) {
-  constexpr int kStep = WARPS_K * kUnroll;
   __shared__ float red[WARPS_K > 1 ? WARPS_N * WARPS_K * MT * 4 * 32 : 1];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wn = warp / WARPS_K, wk = warp % WARPS_K;
-  const int q = lane >> 2, c = lane & 3;
+  TileGeom t;
+  t.q = lane >> 2;
+  t.c = lane & 3;
   const int64_t n0 = (static_cast<int64_t>(blockIdx.x) * WARPS_N + wn) * 16;
-  const int64_t rowA = n0 + q, rowB = n0 + q + 8;
-  const bool okA = rowA < p.N, okB = rowB < p.N;
+  t.rowA = n0 + t.q;
+  t.rowB = n0 + t.q + 8;
+  t.okA = t.rowA < p.N;
+  t.okB = t.rowB < p.N;
   const int nblk = static_cast<int>((p.K + 127) / 128);
   const int b_begin = static_cast<int>(blockIdx.y) * p.blocks_per_split;
-  const int b_end = min(nblk, b_begin + p.blocks_per_split);
+  t.b_end = min(nblk, b_begin + p.blocks_per_split);
   const int64_t ldw = p.K / 8;
-  const int32_t* wA = p.qw + (okA ? rowA : 0) * ldw + 4 * c;
-  const int32_t* wB = p.qw + (okB ? rowB : 0) * ldw + 4 * c;
-  const int64_t m_base = static_cast<int64_t>(blockIdx.z) * (8 * MT);
+  t.wA = p.qw + (t.okA ? t.rowA : 0) * ldw + 4 * t.c;
+  t.wB = p.qw + (t.okB ? t.rowB : 0) * ldw + 4 * t.c;
+  t.m_base = static_cast<int64_t>(blockIdx.z) * (8 * MT);
 
   float acc[MT][4];
 #pragma unroll
@@ -118,38 +170,31 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K)
 #pragma unroll
     for (int r = 0; r < 4; ++r) acc[mt][r] = 0.f;
 
-  auto load_stage = [&](int b, uint4 (&wa)[kUnroll], uint4 (&wb)[kUnroll]) {
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int bb = b + u * WARPS_K;
-      const int64_t k = static_cast<int64_t>(bb) * 128 + 32 * c;
-      const bool kv = bb < b_end && k < p.K;
-      wa[u] = (kv && okA) ? ldg_stream_v4(wA + static_cast<int64_t>(bb) * 16) : make_uint4(0, 0, 0, 0);
-      wb[u] = (kv && okB) ? ldg_stream_v4(wB + static_cast<int64_t>(bb) * 16) : make_uint4(0, 0, 0, 0);
-    }
-  };
-
-  // Weights never depend on the preceding kernel, so the first stage is requested before the
-  // programmatic-dependent-launch wait; activations and every store come after it.
-  uint4 wa[kUnroll], wb[kUnroll];
-  int b = b_begin + wk;
-  load_stage(b, wa, wb);
+  // Three K blocks in flight per warp (register ring). Weights, scales and zero points of the
+  // first three are requested before the programmatic-dependent-launch wait; activations and
+  // every store come after it.
+  constexpr int W = WARPS_K;
+  const int b0 = b_begin + wk;
+  Slot<MT> s0, s1, s2;
+  load_weights(s0, b0, p, t);
+  load_weights(s1, b0 + W, p, t);
+  load_weights(s2, b0 + 2 * W, p, t);
   pdl_wait();
-  for (; b < b_end; b += kStep) {
-    uint4 na[kUnroll], nb[kUnroll];
-    load_stage(b + kStep, na, nb);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int bb = b + u * WARPS_K;
-      const int64_t k = static_cast<int64_t>(bb) * 128 + 32 * c;
-      const bool kv = bb < b_end && k < p.K;
-      mma_block<MT>(acc, wa[u], wb[u], kv, k, p, rowA, rowB, okA, okB, m_base, q);
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      wa[u] = na[u];
-      wb[u] = nb[u];
-    }
+  load_acts(s0, p, t);
+  load_acts(s1, p, t);
+  load_acts(s2, p, t);
+  for (int b = b0; b < t.b_end; b += 3 * W) {
+    mma_slot(acc, s0, p, t);
+    load_weights(s0, b + 3 * W, p, t);
+    load_acts(s0, p, t);
+    if (b + W >= t.b_end) break;
+    mma_slot(acc, s1, p, t);
+    load_weights(s1, b + 4 * W, p, t);
+    load_acts(s1, p, t);
+    if (b + 2 * W >= t.b_end) break;
+    mma_slot(acc, s2, p, t);
+    load_weights(s2, b + 5 * W, p, t);
+    load_acts(s2, p, t);
   }
   pdl_launch_dependents();
 
@@ -178,8 +223,8 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K)
   for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int64_t n = (r < 2) ? rowA : rowB;
-      const int64_t m = m_base + mt * 8 + 2 * c + (r & 1);
+      const int64_t n = (r < 2) ? t.rowA : t.rowB;
+      const int64_t m = t.m_base + mt * 8 + 2 * t.c + (r & 1);
       if (n >= p.N || m >= p.M) continue;
       if (p.split_k == 1) {
         float v = acc[mt][r];
@@ -264,9 +309,15 @@ int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t 
   else
     st = launch_mt<8>(plan, p, stream, pdl);
   if (st != TF_OK || plan.split_k == 1) return st;
-  const int64_t MN = a.M * a.N;
+  return launch_splitk_reduce(p.partial, plan.split_k, a.M, a.N, a.bias, a.y, a.ldy, stream);
+}
+
+int launch_splitk_reduce(const float* partial, int split, int64_t M, int64_t N,
+                         const uint16_t* bias, uint16_t* y, int64_t ldy, cudaStream_t stream) {
+  const int64_t MN = M * N;
   splitk_reduce_kernel<<<static_cast<unsigned>(cdiv(MN, 256)), 256, 0, stream>>>(
-      p.partial, plan.split_k, a.M, a.N, p.bias, p.y, a.ldy);
+      partial, split, M, N, reinterpret_cast<const __half*>(bias), reinterpret_cast<__half*>(y),
+      ldy);
   return check_launch();
 }
 
