@@ -68,14 +68,26 @@ def test_prefill_sizes_use_a_gemm(m: int) -> None:
                                       (200, 256), (1000, 1024), (896, 4864), (1152, 896)])
 def test_plan_covers_every_k_block_once(n: int, k: int) -> None:
     plan = launch_plan(1, n, k, 128)
-    kblocks = -(-k // 128)
+    assert plan.kernel == "gemv"
+    kblocks = -(-k // 256)  # the decode GEMV walks 256-wide K blocks
     assert plan.warps_k in (1, 2, 4, 8)
     assert plan.grid_x * (8 // plan.warps_k) * 16 >= n
     assert 1 <= plan.split_k <= 8
     per = -(-kblocks // plan.split_k)
     assert (plan.split_k - 1) * per < kblocks <= plan.split_k * per  # no empty split
     ws = workspace_bytes(1, n, k, 128)
-    assert ws == (plan.split_k * n * 4 if plan.split_k > 1 else 0)
+    assert ws >= (plan.split_k * n * 4 if plan.split_k > 1 else 0)
+
+
+@pytest.mark.parametrize(("m", "n", "k"), [(1024, 3584, 18944), (64, 3584, 18944), (16, 37888, 3584)])
+def test_tensor_core_plan_splits_k_to_fill_the_gpu(m: int, n: int, k: int) -> None:
+    plan = launch_plan(m, n, k, 128)
+    assert plan.kernel == "tcgen05_gemm"
+    base = plan.grid_x * plan.grid_z
+    units = base * plan.split_k
+    # Splitting K must not make the busiest persistent CTA's share of the work larger.
+    assert -(-units // 148) / plan.split_k <= -(-base // 148)
+    assert workspace_bytes(m, n, k, 128) >= (plan.split_k * m * n * 4 if plan.split_k > 1 else 0)
 
 
 def test_plan_is_deterministic() -> None:

@@ -40,9 +40,42 @@ constexpr BucketEntry kTable[] = {
     {4096, kKernelTcGemm, 256}, {1 << 30, kKernelTcGemm, 256},
 };
 
+// Decode GEMV: 16-row warp tiles over 256-wide K blocks. Warps per tile (1..8) is the smallest
+// power of two that puts two CTAs' worth of warps on every SM, as long as each warp keeps at
+// least 1.5 blocks. K is split across CTAs (fp32 partials + a reduce launch) only when the tiles
+// cannot give every SM one CTA and each warp would still stream 8+ blocks, or when the staged
+// activations would not fit in 100 KB of shared memory.
+int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
+  pl->tile_m = 8;
+  pl->tile_n = 16;
+  const int64_t n_tiles = cdiv(N, 16);
+  const int64_t kblocks = cdiv(K, 256);
+  int wk = 1;
+  while (wk < 8 && n_tiles * wk < 2 * 8 * kNumSms && 3 * (2 * wk) <= 2 * kblocks) wk *= 2;
+  pl->warps_k = wk;
+  const int64_t gx = cdiv(n_tiles, 8 / wk);
+  int64_t split = 1;
+  if (n_tiles * wk < 8 * kNumSms && kblocks >= 8 * wk) {
+    split = std::min<int64_t>(8, cdiv(2 * 8 * kNumSms, n_tiles * wk));
+    split = std::max<int64_t>(1, std::min<int64_t>(split, kblocks / (4 * wk)));
+  }
+  const int64_t max_bps = std::max<int64_t>(1, ((100 * 1024) / (2 * M) - 8) / 256);
+  split = std::max<int64_t>(split, cdiv(kblocks, max_bps));
+  const int64_t per = cdiv(kblocks, split);
+  split = cdiv(kblocks, per);
+  if (gx > 0x7fffffffLL || split > 65535) return TF_ERR_UNSUPPORTED;
+  pl->split_k = static_cast<int>(split);
+  pl->blocks_per_split = static_cast<int>(per);
+  pl->grid_x = static_cast<unsigned>(gx);
+  pl->grid_y = static_cast<unsigned>(split);
+  pl->grid_z = 1;
+  pl->workspace = split > 1 ? static_cast<size_t>(split * M * N) * sizeof(float) : 0;
+  return TF_OK;
+}
+
+// 64-token warp-MMA tiles: 16-row warp tiles, 128-wide K blocks split over up to 8 warps.
 int plan_mma(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
-  const int mt_tokens = pl->kernel == kKernelGemv ? 8 : 64;
-  pl->tile_m = mt_tokens;
+  pl->tile_m = 64;
   pl->tile_n = 16;
   const int64_t n_tiles = cdiv(N, 16);
   const int64_t kblocks = cdiv(K, 128);
@@ -51,7 +84,7 @@ int plan_mma(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   pl->warps_k = wk;
   const int wn = 8 / wk;
   const int64_t gx = cdiv(n_tiles, wn);
-  const int64_t gz = cdiv(M, mt_tokens);
+  const int64_t gz = cdiv(M, 64);
   const int64_t ctas = gx * gz;
   int64_t split = 1;
   if (ctas < kNumSms && kblocks >= 4 * wk) {
@@ -71,6 +104,12 @@ int plan_mma(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   return TF_OK;
 }
 
+// The decode GEMV indexes with 32-bit integers.
+bool gemv_fits(int64_t M, int64_t N, int64_t K, int64_t ldx, int group_size) {
+  const int64_t lim = int64_t(1) << 31;
+  return N * (K / 8) < lim && (K / group_size + 1) * N < lim && M * ldx < lim && K < lim;
+}
+
 }  // namespace
 
 uint32_t launch_flags() { return g_launch_flags; }
@@ -86,11 +125,14 @@ int plan_linear(int64_t M, int64_t N, int64_t K, int group_size, LinearPlan* pl)
   pl->kernel = kTable[idx].kernel;
   if (pl->kernel == kKernelTcGemm && !tc_gemm_supported(M, N, K, group_size))
     pl->kernel = kKernelMmaGemm;
+  if (pl->kernel == kKernelGemv && !gemv_fits(M, N, K, K, group_size))
+    pl->kernel = kKernelMmaGemm;
   if (pl->kernel == kKernelTcGemm) {
     pl->tile_m = kTable[idx].tile_m;
     plan_tc(M, N, K, pl);
     return TF_OK;
   }
+  if (pl->kernel == kKernelGemv) return plan_gemv(M, N, K, pl);
   return plan_mma(M, N, K, pl);
 }
 
@@ -127,10 +169,16 @@ int run_linear(const LinearArgs& a, cudaStream_t stream, int force_kernel) {
       plan_tc(a.M, a.N, a.K, &pl);
     }
   }
+  if (pl.kernel == kKernelGemv && !gemv_fits(a.M, a.N, a.K, a.ldx, a.group_size)) {
+    pl.kernel = kKernelMmaGemm;
+    st = plan_mma(a.M, a.N, a.K, &pl);
+    if (st != TF_OK) return st;
+  }
   if (pl.workspace > 0 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace))
     return TF_ERR_WORKSPACE;
   if (pl.kernel == kKernelTcGemm) return launch_tc_gemm(pl, a, stream);
-  return launch_mma_linear(pl, a, stream);
+  if (pl.kernel == kKernelGemv) return launch_gemv(pl, a, stream);
+  return launch_mma_tiles(pl, a, stream);
 }
 
 LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const int32_t* qw,
@@ -186,9 +234,14 @@ size_t tf_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_s
   if (tfb::plan_linear(M, N, K, group_size, &pl) != TF_OK) return 0;
   // The GEMM entry may fall back to the 64-token MMA kernel; size for the larger of the two.
   tfb::LinearPlan alt = pl;
-  alt.kernel = tfb::kKernelMmaGemm;
   size_t ws = pl.workspace;
   if (tfb::plan_mma(M, N, K, &alt) == TF_OK && alt.workspace > ws) ws = alt.workspace;
+  if (M <= 8 && tfb::plan_gemv(M, N, K, &alt) == TF_OK && alt.workspace > ws) ws = alt.workspace;
+  if (tfb::tc_gemm_supported(M, N, K, group_size)) {
+    alt.tile_m = 16;
+    tfb::plan_tc(M, N, K, &alt);
+    if (alt.workspace > ws) ws = alt.workspace;
+  }
   return ws;
 }
 

@@ -8,7 +8,7 @@
 namespace tfb {
 
 enum LinearKernel : int {
-  kKernelGemv = 0,     // warp-level MMA, one 8-token tile (M <= 8)
+  kKernelGemv = 0,     // decode GEMV (M <= 8): activations in shared memory, warp-level MMA
   kKernelMmaGemm = 1,  // warp-level MMA, 64-token tiles
   kKernelTcGemm = 2,   // tcgen05 + TMEM + TMA tensor-core GEMM
 };
@@ -20,7 +20,7 @@ struct LinearPlan {
   int warps_k;           // warps splitting K inside one CTA (mma kernels)
   int split_k;           // CTAs splitting K (partials reduced in a fixed order)
   int tile_m;            // tokens per CTA tile
-  int blocks_per_split;  // 128-wide K blocks per split (mma kernels)
+  int blocks_per_split;  // K blocks per split: 256 wide (GEMV), 128 (MMA tiles), 64 (tcgen05)
   unsigned grid_x, grid_y, grid_z;
   size_t workspace;      // bytes of scratch the launch needs
 };
@@ -46,7 +46,10 @@ struct LinearArgs {
   size_t workspace_bytes;
 };
 
-int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+int launch_mma_tiles(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+// Dynamic shared memory of the decode GEMV: M staged activation rows of bps * 256 (+8) fp16.
+size_t gemv_smem_bytes(int64_t M, int bps);
 int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size);
 // Fills split_k / blocks_per_split / grid / workspace of a tensor-core plan whose tile_m is set.

@@ -1,37 +1,39 @@
-// W4A16 linear on the warp-level tensor-core path: decode GEMV (M <= 8) and a 64-token tiled
-// variant. y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]) with w = fp16(q - z) * s.
+// W4A16 decode GEMV for M = 1..8: y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]),
+// w = fp16(q - z) * s rounded once, fp32 accumulation, fp16 output.
 //
-// Reference semantics: triton/w4a16.py:44-115 (in-register dequant with one fp16 rounding,
-// fp32 accumulation, fp16 output, bias added in fp32 before the cast) and the split-K contract
-// of w4a16.py:193-200,227-232 (fp32 partials summed in a fixed order, then bias, then cast).
+// Reference semantics: tokenforge/kernels/triton/w4a16.py:44-115 (the BLOCK_M == 1 / small-M
+// paths) and its split-K contract w4a16.py:193-200,227-232 (fp32 partials summed in a fixed
+// order, then bias, then the cast). Replaces the planned `_C.w4a16_gemv` (ops.py:86-88).
 //
-// Why tensor cores for a GEMV: at M = 1 the kernel must turn ~13e12 int4 weights per second
-// into products to keep pace with HBM. Dequantizing with the exact reference rounding already
-// costs ~2 instructions per weight (LOP3 + HSUB2 + HMUL2 per fp16 pair, plus shifts), which is
-// most of the SM's issue budget; an fp32 FMA per weight on top would make the kernel ALU-bound
-// below the HBM roofline. So the warp dequantizes straight into mma.m16n8k16 A fragments and
-// the tensor core performs the fp32 multiply-accumulate, for any M from 1 to 8 at the same
-// instruction cost.
-//
-// Tiling. A warp owns 16 weight rows (n0..n0+15) and a strided subset of 128-wide K blocks.
-// Lane L = 4*q + c loads a 16-byte vector of row n0+q and of row n0+q+8 covering k in
-// [128b + 32c, 128b + 32c + 32): the 4 lanes of a quad read 64 contiguous bytes of each row.
-// Each packed word (8 values of k) yields two m16n8k16 steps. The tensor core sums over the 16
-// "logical" k of a step, so the logical-to-actual k mapping only has to agree between the A
-// fragment (weights) and the B fragment (activations): word pairs 0,1 -> step 0 and pairs 2,3 ->
-// step 1, which makes the B fragment of lane L exactly the 16 bytes x[m][k..k+7] of its own
-// chunk (m = L/4). No shuffles, no shared-memory staging of the weights.
-//
-// Accumulators of the WARPS_K warps that split K are reduced through shared memory in warp
-// order; cross-CTA split-K writes fp32 partials to the workspace and a second kernel reduces
-// them in split order. Deterministic: graph replay and eager runs are bit-identical.
+// The kernel is bound by the instructions that dequantize weights exactly (HSUB2 + HMUL2 per
+// fp16 pair run at half rate on B200), so everything else is kept out of the inner loop:
+//   * the CTA's activations x[0:M, k-range] are staged once in shared memory, so a K block costs
+//     the warp one 16-byte shared load per packed word and no global address arithmetic;
+//   * a warp owns 16 weight rows and walks 256-wide K blocks; lane L = 4q + c loads 32 bytes of
+//     row n0+q and of row n0+q+8 (k in [256b + 64c, +64)), so each quad reads 128 contiguous bytes
+//     per row, and three blocks (weights, scales, zero points) are in flight per warp in a
+//     register ring, the first three requested before the programmatic-dependent-launch wait;
+//   * rows beyond N and tokens beyond M are clamped for loading (never stored) instead of
+//     predicated; only a partial last K block takes predicated loads;
+//   * each packed word is unpacked with one shift: pairs 0 and 2 come from the mask 0x000F000F
+//     of w and w >> 8 (fp16 1024 + q), pairs 1 and 3 from the mask 0x00F000F0 (1024 + 16q), whose
+//     difference with 1024 + 16z is 16(q - z) exactly and is multiplied by the exact s/16, so both
+//     give the reference's correctly rounded fp16(q - z) * s. When a scale in the warp is too
+//     small for s/16 to be exact, the block takes the three-shift unpack instead (warp vote).
+// The dequantized pairs feed mma.m16n8k16 A fragments directly (the k order inside a step only
+// has to agree between A and B); the tensor core does the fp32 multiply-accumulate.
+// Warps that split K inside a CTA are summed through shared memory in warp order; CTAs that split
+// K write fp32 partials reduced by a second kernel in split order: bit-identical on every run.
 #include "tf_common.cuh"
 #include "tf_plan.h"
 
 namespace tfb {
 namespace {
 
-struct MmaParams {
+constexpr int kKB = 256;       // K values per block
+constexpr int kCtaWarps = 8;   // warps per CTA (WARPS_N x WARPS_K)
+
+struct GemvParams {
   const __half* x;
   int64_t ldx;
   const int32_t* qw;
@@ -41,198 +43,277 @@ struct MmaParams {
   __half* y;
   int64_t ldy;
   float* partial;  // [split_k, M, N] fp32 when split_k > 1
-  int64_t M, N, K;
-  int group_size;
+  int M, N, K;
+  int group_shift;  // log2(group size)
   int split_k;
-  int blocks_per_split;
+  int bps;          // 256-wide K blocks per split
+  int xs_stride;    // fp16 elements per staged activation row
 };
 
-// One K block (128 values of k) of one warp tile, as held in registers between the moment its
-// loads are issued and the moment it is consumed.
-template <int MT>
-struct Slot {
-  uint4 wa, wb;                 // packed weights of rows A = n0+q and B = n0+q+8 (16 B each)
-  __half sa, sb;                // scales of the block's group for rows A and B
-  uint32_t za, zb;              // qzeros words holding the rows' zero points
-  uint4 x[MT == 1 ? 4 : 1];     // activations x[q][k..k+31] (decode tile only)
-  int64_t k;                    // first k of this lane's 32-value chunk
-  bool kv;                      // the block exists (k < K and inside this CTA's K range)
+// One K block of a warp tile in registers: this lane's 64 values of k for two weight rows.
+struct GSlot {
+  uint4 wa0, wa1, wb0, wb1;      // rows A and B: words 0-3 and 4-7 of the lane's chunk
+  uint32_t s0, s1;               // scales (row A | row B << 16) of the chunk's two 32-k halves
+  uint32_t za0, zb0, za1, zb1;   // qzeros words of those halves
 };
 
-struct TileGeom {
-  int64_t rowA, rowB, m_base;
-  bool okA, okB;
-  int q, c, b_end;
-  const int32_t* wA;
+struct GLane {
+  const int32_t* wA;   // packed row A + this lane's word offset 8c
   const int32_t* wB;
+  const __half* sA;    // scales + row A
+  const __half* sB;
+  const int32_t* zA;   // qzeros + row A / 8
+  const int32_t* zB;
+  const uint4* xs;     // staged activations: token row q (clamped), + 64c
+  int nibA, nibB;
+  int kb0, b_end;      // this CTA's first block, this warp's end block (exclusive)
+  int c;
 };
 
-// Weights, scales and zero points: never written by the preceding kernel, so these loads may be
-// issued before the programmatic-dependent-launch wait.
-template <int MT>
-__device__ __forceinline__ void load_weights(Slot<MT>& s, int bb, const MmaParams& p,
-                                             const TileGeom& t) {
-  s.k = static_cast<int64_t>(bb) * 128 + 32 * t.c;
-  s.kv = bb < t.b_end && s.k < p.K;
-  const uint4 zero = make_uint4(0, 0, 0, 0);
-  s.wa = (s.kv && t.okA) ? ldg_stream_v4(t.wA + static_cast<int64_t>(bb) * 16) : zero;
-  s.wb = (s.kv && t.okB) ? ldg_stream_v4(t.wB + static_cast<int64_t>(bb) * 16) : zero;
-  s.sa = s.sb = __ushort_as_half(0);
-  s.za = s.zb = 0;
-  if (s.kv) {
-    const int64_t g = s.k / p.group_size;
-    if (t.okA) {
-      s.sa = __ldg(p.scales + g * p.N + t.rowA);
-      s.za = static_cast<uint32_t>(__ldg(p.qzeros + g * (p.N / 8) + (t.rowA >> 3)));
+__device__ __forceinline__ uint4 zero4() { return make_uint4(0, 0, 0, 0); }
+
+template <bool kTwo>
+__device__ __forceinline__ void gload(GSlot& s, int bb, const GemvParams& p, const GLane& L) {
+  if (bb >= L.b_end) return;  // warp-uniform: the slot is never consumed
+  const int wo = bb * (kKB / 8);
+  const int k = bb * kKB + 64 * L.c;
+  const int g0 = k >> p.group_shift;
+  const int n8 = p.N >> 3;
+  const uint4* pa = reinterpret_cast<const uint4*>(L.wA + wo);
+  const uint4* pb = reinterpret_cast<const uint4*>(L.wB + wo);
+  if ((bb + 1) * kKB <= p.K) {
+    s.wa0 = ldg_stream_v4(pa);
+    s.wa1 = ldg_stream_v4(pa + 1);
+    s.wb0 = ldg_stream_v4(pb);
+    s.wb1 = ldg_stream_v4(pb + 1);
+    s.s0 = __half_as_ushort(__ldg(L.sA + g0 * p.N)) |
+           (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g0 * p.N))) << 16);
+    s.za0 = static_cast<uint32_t>(__ldg(L.zA + g0 * n8));
+    s.zb0 = static_cast<uint32_t>(__ldg(L.zB + g0 * n8));
+    if constexpr (kTwo) {
+      const int g1 = g0 + 1;
+      s.s1 = __half_as_ushort(__ldg(L.sA + g1 * p.N)) |
+             (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g1 * p.N))) << 16);
+      s.za1 = static_cast<uint32_t>(__ldg(L.zA + g1 * n8));
+      s.zb1 = static_cast<uint32_t>(__ldg(L.zB + g1 * n8));
     }
-    if (t.okB) {
-      s.sb = __ldg(p.scales + g * p.N + t.rowB);
-      s.zb = static_cast<uint32_t>(__ldg(p.qzeros + g * (p.N / 8) + (t.rowB >> 3)));
+  } else {  // partial last block: halves past K contribute exact zeros (s = 0, z = 0, q = 0)
+    const bool in0 = k < p.K, in1 = k + 32 < p.K;
+    s.wa0 = in0 ? ldg_stream_v4(pa) : zero4();
+    s.wa1 = in1 ? ldg_stream_v4(pa + 1) : zero4();
+    s.wb0 = in0 ? ldg_stream_v4(pb) : zero4();
+    s.wb1 = in1 ? ldg_stream_v4(pb + 1) : zero4();
+    s.s0 = in0 ? (__half_as_ushort(__ldg(L.sA + g0 * p.N)) |
+                  (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g0 * p.N))) << 16))
+               : 0u;
+    s.za0 = in0 ? static_cast<uint32_t>(__ldg(L.zA + g0 * n8)) : 0u;
+    s.zb0 = in0 ? static_cast<uint32_t>(__ldg(L.zB + g0 * n8)) : 0u;
+    if constexpr (kTwo) {
+      const int g1 = g0 + 1;
+      s.s1 = in1 ? (__half_as_ushort(__ldg(L.sA + g1 * p.N)) |
+                    (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g1 * p.N))) << 16))
+                 : 0u;
+      s.za1 = in1 ? static_cast<uint32_t>(__ldg(L.zA + g1 * n8)) : 0u;
+      s.zb1 = in1 ? static_cast<uint32_t>(__ldg(L.zB + g1 * n8)) : 0u;
+    } else if (!in1) {
+      // Group size >= 64: both halves share one group; a missing second half still needs s = 0.
+      s.s1 = 0u;
+      s.za1 = s.zb1 = 0u;
     }
   }
-}
-
-// Activations (decode tile only; the 64-token tile reads them while computing).
-template <int MT>
-__device__ __forceinline__ void load_acts(Slot<MT>& s, const MmaParams& p, const TileGeom& t) {
-  if constexpr (MT == 1) {
-    const int64_t m = t.m_base + t.q;
-    const bool ok = s.kv && m < p.M;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      s.x[i] = ok ? ldg_v4(p.x + m * p.ldx + s.k + 8 * i) : make_uint4(0, 0, 0, 0);
-  }
-}
-
-template <int MT>
-__device__ __forceinline__ void mma_slot(float (&acc)[MT][4], const Slot<MT>& s,
-                                         const MmaParams& p, const TileGeom& t) {
-  const int nibA = 4 * awq_nibble_of(static_cast<int>(t.rowA & 7));
-  const int nibB = 4 * awq_nibble_of(static_cast<int>(t.rowB & 7));
-  const __half2 zzA = zero_magic2((s.za >> nibA) & 0xFu);
-  const __half2 zzB = zero_magic2((s.zb >> nibB) & 0xFu);
-  const __half2 ssA = __halves2half2(s.sa, s.sa);
-  const __half2 ssB = __halves2half2(s.sb, s.sb);
-  const uint32_t wa_w[4] = {s.wa.x, s.wa.y, s.wa.z, s.wa.w};
-  const uint32_t wb_w[4] = {s.wb.x, s.wb.y, s.wb.z, s.wb.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t a0[4] = {dequant_pair(magic_pair(wa_w[i], 0), zzA, ssA),
-                            dequant_pair(magic_pair(wb_w[i], 0), zzB, ssB),
-                            dequant_pair(magic_pair(wa_w[i], 1), zzA, ssA),
-                            dequant_pair(magic_pair(wb_w[i], 1), zzB, ssB)};
-    const uint32_t a1[4] = {dequant_pair(magic_pair(wa_w[i], 2), zzA, ssA),
-                            dequant_pair(magic_pair(wb_w[i], 2), zzB, ssB),
-                            dequant_pair(magic_pair(wa_w[i], 3), zzA, ssA),
-                            dequant_pair(magic_pair(wb_w[i], 3), zzB, ssB)};
-    if constexpr (MT == 1) {
-      mma_16816(acc[0], a0, s.x[i].x, s.x[i].y);
-      mma_16816(acc[0], a1, s.x[i].z, s.x[i].w);
-    } else {
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int64_t m = t.m_base + mt * 8 + t.q;
-        uint4 xv = make_uint4(0, 0, 0, 0);
-        if (s.kv && m < p.M) xv = ldg_v4(p.x + m * p.ldx + s.k + 8 * i);
-        mma_16816(acc[mt], a0, xv.x, xv.y);
-        mma_16816(acc[mt], a1, xv.z, xv.w);
-      }
+  if constexpr (!kTwo) {
+    if ((bb + 1) * kKB <= p.K || k + 32 < p.K) {
+      s.s1 = s.s0;
+      s.za1 = s.za0;
+      s.zb1 = s.zb0;
     }
   }
 }
 
-template <int MT, int WARPS_N, int WARPS_K>
-__global__ void __launch_bounds__(32 * WARPS_N * WARPS_K)
-    w4a16_mma_kernel(const MmaParams p) {
-  __shared__ float red[WARPS_K > 1 ? WARPS_N * WARPS_K * MT * 4 * 32 : 1];
+// A scale s admits the one-shift unpack iff s/16 is exact in fp16: zero, non-finite, or at
+// least 2^-10 in magnitude.
+__device__ __forceinline__ bool splits_exactly(uint32_t h) {
+  const uint32_t mag = h & 0x7FFFu;
+  return mag == 0u || mag >= 0x1400u;
+}
+
+__device__ __forceinline__ __half2 lo2(uint32_t s) {
+  const __half h = __ushort_as_half(static_cast<unsigned short>(s & 0xFFFFu));
+  return __halves2half2(h, h);
+}
+__device__ __forceinline__ __half2 hi2(uint32_t s) {
+  const __half h = __ushort_as_half(static_cast<unsigned short>(s >> 16));
+  return __halves2half2(h, h);
+}
+
+struct HalfConsts {  // per 32-k half of a chunk: zero-point magics and scales for rows A and B
+  __half2 z1A, z1B, z16A, z16B, s1A, s1B, s16A, s16B;
+};
+
+__device__ __forceinline__ HalfConsts make_consts(uint32_t s, uint32_t za_w, uint32_t zb_w,
+                                                  const GLane& L) {
+  HalfConsts h;
+  const uint32_t za = (za_w >> L.nibA) & 0xFu, zb = (zb_w >> L.nibB) & 0xFu;
+  h.z1A = zero_magic2(za);
+  h.z1B = zero_magic2(zb);
+  h.z16A = u32_as_h2(0x64006400u | (za << 4) | (za << 20));
+  h.z16B = u32_as_h2(0x64006400u | (zb << 4) | (zb << 20));
+  h.s1A = lo2(s);
+  h.s1B = hi2(s);
+  const __half2 sixteenth = __float2half2_rn(0.0625f);
+  h.s16A = __hmul2(h.s1A, sixteenth);
+  h.s16B = __hmul2(h.s1B, sixteenth);
+  return h;
+}
+
+__device__ __forceinline__ void word_fast(float (&acc)[4], uint32_t wa, uint32_t wb,
+                                          const HalfConsts& h, const uint4& xv) {
+  const uint32_t a8 = wa >> 8, b8 = wb >> 8;
+  const uint32_t f0[4] = {dequant_pair((wa & 0x000F000Fu) | 0x64006400u, h.z1A, h.s1A),
+                          dequant_pair((wb & 0x000F000Fu) | 0x64006400u, h.z1B, h.s1B),
+                          dequant_pair((wa & 0x00F000F0u) | 0x64006400u, h.z16A, h.s16A),
+                          dequant_pair((wb & 0x00F000F0u) | 0x64006400u, h.z16B, h.s16B)};
+  const uint32_t f1[4] = {dequant_pair((a8 & 0x000F000Fu) | 0x64006400u, h.z1A, h.s1A),
+                          dequant_pair((b8 & 0x000F000Fu) | 0x64006400u, h.z1B, h.s1B),
+                          dequant_pair((a8 & 0x00F000F0u) | 0x64006400u, h.z16A, h.s16A),
+                          dequant_pair((b8 & 0x00F000F0u) | 0x64006400u, h.z16B, h.s16B)};
+  mma_16816(acc, f0, xv.x, xv.y);
+  mma_16816(acc, f1, xv.z, xv.w);
+}
+
+__device__ __forceinline__ void word_exact(float (&acc)[4], uint32_t wa, uint32_t wb,
+                                           const HalfConsts& h, const uint4& xv) {
+  const uint32_t f0[4] = {dequant_pair(magic_pair(wa, 0), h.z1A, h.s1A),
+                          dequant_pair(magic_pair(wb, 0), h.z1B, h.s1B),
+                          dequant_pair(magic_pair(wa, 1), h.z1A, h.s1A),
+                          dequant_pair(magic_pair(wb, 1), h.z1B, h.s1B)};
+  const uint32_t f1[4] = {dequant_pair(magic_pair(wa, 2), h.z1A, h.s1A),
+                          dequant_pair(magic_pair(wb, 2), h.z1B, h.s1B),
+                          dequant_pair(magic_pair(wa, 3), h.z1A, h.s1A),
+                          dequant_pair(magic_pair(wb, 3), h.z1B, h.s1B)};
+  mma_16816(acc, f0, xv.x, xv.y);
+  mma_16816(acc, f1, xv.z, xv.w);
+}
+
+template <bool kTwo>
+__device__ __forceinline__ void gcompute(float (&acc)[4], const GSlot& s, int bb,
+                                         const GLane& L, int K) {
+  const uint4* xp = L.xs + (bb - L.kb0) * (kKB / 8);
+  const bool fast = __all_sync(0xffffffffu, splits_exactly(s.s0 & 0xFFFFu) &&
+                                                splits_exactly(s.s0 >> 16) &&
+                                                splits_exactly(s.s1 & 0xFFFFu) &&
+                                                splits_exactly(s.s1 >> 16));
+  // The second 32-k half has its own scale / zero point when the group size is 32, and in a
+  // partial last block (where a half past K carries s = 0, z = 0 so it adds exact zeros).
+  const bool partial = (bb + 1) * kKB > K;  // warp-uniform
+  const HalfConsts h0 = make_consts(s.s0, s.za0, s.zb0, L);
+  const HalfConsts h1 = (kTwo || partial) ? make_consts(s.s1, s.za1, s.zb1, L) : h0;
+  const uint32_t wa[8] = {s.wa0.x, s.wa0.y, s.wa0.z, s.wa0.w, s.wa1.x, s.wa1.y, s.wa1.z, s.wa1.w};
+  const uint32_t wb[8] = {s.wb0.x, s.wb0.y, s.wb0.z, s.wb0.w, s.wb1.x, s.wb1.y, s.wb1.z, s.wb1.w};
+  if (fast) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) word_fast(acc, wa[j], wb[j], j < 4 ? h0 : h1, xp[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) word_exact(acc, wa[j], wb[j], j < 4 ? h0 : h1, xp[j]);
+  }
+}
+
+template <int WARPS_N, int WARPS_K, bool kTwo>
+__global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const GemvParams p) {
+  static_assert(WARPS_N * WARPS_K == kCtaWarps, "CTA shape");
+  extern __shared__ uint4 xs_smem[];
+  __shared__ float red[kCtaWarps * 4 * 32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wn = warp / WARPS_K, wk = warp % WARPS_K;
-  TileGeom t;
-  t.q = lane >> 2;
-  t.c = lane & 3;
-  const int64_t n0 = (static_cast<int64_t>(blockIdx.x) * WARPS_N + wn) * 16;
-  t.rowA = n0 + t.q;
-  t.rowB = n0 + t.q + 8;
-  t.okA = t.rowA < p.N;
-  t.okB = t.rowB < p.N;
-  const int nblk = static_cast<int>((p.K + 127) / 128);
-  const int b_begin = static_cast<int>(blockIdx.y) * p.blocks_per_split;
-  t.b_end = min(nblk, b_begin + p.blocks_per_split);
+  const int q = lane >> 2;
+  GLane L;
+  L.c = lane & 3;
+  const int n0 = (blockIdx.x * WARPS_N + wn) * 16;
+  const int rowA = n0 + q, rowB = n0 + q + 8;
+  const int ra = min(rowA, p.N - 1), rb = min(rowB, p.N - 1);
+  const int nblk = (p.K + kKB - 1) / kKB;
+  L.kb0 = blockIdx.y * p.bps;
+  const int kb1 = min(nblk, L.kb0 + p.bps);
+  L.b_end = kb1;
   const int64_t ldw = p.K / 8;
-  t.wA = p.qw + (t.okA ? t.rowA : 0) * ldw + 4 * t.c;
-  t.wB = p.qw + (t.okB ? t.rowB : 0) * ldw + 4 * t.c;
-  t.m_base = static_cast<int64_t>(blockIdx.z) * (8 * MT);
+  L.wA = p.qw + ra * ldw + 8 * L.c;
+  L.wB = p.qw + rb * ldw + 8 * L.c;
+  L.sA = p.scales + ra;
+  L.sB = p.scales + rb;
+  L.zA = p.qzeros + (ra >> 3);
+  L.zB = p.qzeros + (rb >> 3);
+  L.nibA = 4 * awq_nibble_of(ra & 7);
+  L.nibB = 4 * awq_nibble_of(rb & 7);
+  const int xq = min(q, p.M - 1);
+  L.xs = xs_smem + (xq * p.xs_stride + 64 * L.c) / 8;
 
-  float acc[MT][4];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) acc[mt][r] = 0.f;
-
-  // Three K blocks in flight per warp (register ring). Weights, scales and zero points of the
-  // first three are requested before the programmatic-dependent-launch wait; activations and
-  // every store come after it.
+  // Weights, scales and zero points of the first three blocks do not depend on the preceding
+  // kernel: request them before the programmatic-dependent-launch wait.
+  const int b0 = L.kb0 + wk;
   constexpr int W = WARPS_K;
-  const int b0 = b_begin + wk;
-  Slot<MT> s0, s1, s2;
-  load_weights(s0, b0, p, t);
-  load_weights(s1, b0 + W, p, t);
-  load_weights(s2, b0 + 2 * W, p, t);
+  GSlot s0, s1, s2;
+  gload<kTwo>(s0, b0, p, L);
+  gload<kTwo>(s1, b0 + W, p, L);
+  gload<kTwo>(s2, b0 + 2 * W, p, L);
   pdl_wait();
-  load_acts(s0, p, t);
-  load_acts(s1, p, t);
-  load_acts(s2, p, t);
-  for (int b = b0; b < t.b_end; b += 3 * W) {
-    mma_slot(acc, s0, p, t);
-    load_weights(s0, b + 3 * W, p, t);
-    load_acts(s0, p, t);
-    if (b + W >= t.b_end) break;
-    mma_slot(acc, s1, p, t);
-    load_weights(s1, b + 4 * W, p, t);
-    load_acts(s1, p, t);
-    if (b + 2 * W >= t.b_end) break;
-    mma_slot(acc, s2, p, t);
-    load_weights(s2, b + 5 * W, p, t);
-    load_acts(s2, p, t);
+
+  // Stage x[0:M, kb0*256 : kb1*256] (zero past K) in shared memory.
+  {
+    const int vec_per_row = (kb1 - L.kb0) * (kKB / 8);
+    const int total = p.M * vec_per_row;
+    const int k_lo = L.kb0 * kKB;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int m = i / vec_per_row, v = i - m * vec_per_row;
+      const int k = k_lo + 8 * v;
+      const uint4 val = k < p.K ? ldg_v4(p.x + m * p.ldx + k) : zero4();
+      xs_smem[(m * p.xs_stride) / 8 + v] = val;
+    }
+  }
+  __syncthreads();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int b = b0; b < L.b_end; b += 3 * W) {
+    gcompute<kTwo>(acc, s0, b, L, p.K);
+    gload<kTwo>(s0, b + 3 * W, p, L);
+    if (b + W >= L.b_end) break;
+    gcompute<kTwo>(acc, s1, b + W, L, p.K);
+    gload<kTwo>(s1, b + 4 * W, p, L);
+    if (b + 2 * W >= L.b_end) break;
+    gcompute<kTwo>(acc, s2, b + 2 * W, L, p.K);
+    gload<kTwo>(s2, b + 5 * W, p, L);
   }
   pdl_launch_dependents();
 
   if constexpr (WARPS_K > 1) {
-    float* mine = red + ((wn * WARPS_K + wk) * MT * 4) * 32;
+    float* mine = red + (warp * 4) * 32;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) mine[(mt * 4 + r) * 32 + lane] = acc[mt][r];
+    for (int r = 0; r < 4; ++r) mine[r * 32 + lane] = acc[r];
     __syncthreads();
     if (wk != 0) return;
-    const float* base = red + (wn * WARPS_K * MT * 4) * 32;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < WARPS_K; ++w) s += base[(w * MT * 4 + mt * 4 + r) * 32 + lane];
-        acc[mt][r] = s;
-      }
-  }
-
-  // C fragment: c0,c1 -> row q, tokens 2c, 2c+1; c2,c3 -> row q+8, same tokens.
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
+    const float* base = red + (wn * WARPS_K * 4) * 32;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int64_t n = (r < 2) ? t.rowA : t.rowB;
-      const int64_t m = t.m_base + mt * 8 + 2 * t.c + (r & 1);
-      if (n >= p.N || m >= p.M) continue;
-      if (p.split_k == 1) {
-        float v = acc[mt][r];
-        if (p.bias) v += __half2float(__ldg(p.bias + n));
-        p.y[m * p.ldy + n] = __float2half_rn(v);
-      } else {
-        p.partial[(static_cast<int64_t>(blockIdx.y) * p.M + m) * p.N + n] = acc[mt][r];
-      }
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS_K; ++w) v += base[(w * 4 + r) * 32 + lane];
+      acc[r] = v;
+    }
+  }
+
+  // C fragment: acc[0..1] -> row A, tokens 2c, 2c+1; acc[2..3] -> row B, same tokens.
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int n = (r < 2) ? rowA : rowB;
+    const int m = 2 * L.c + (r & 1);
+    if (n >= p.N || m >= p.M) continue;
+    if (p.split_k == 1) {
+      float v = acc[r];
+      if (p.bias) v += __half2float(__ldg(p.bias + n));
+      p.y[m * p.ldy + n] = __float2half_rn(v);
+    } else {
+      p.partial[(static_cast<int64_t>(blockIdx.y) * p.M + m) * p.N + n] = acc[r];
     }
   }
 }
@@ -252,19 +333,29 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   y[m * ldy + n] = __float2half_rn(s);
 }
 
-template <int MT, int WN, int WK>
-int launch_variant(const LinearPlan& plan, const MmaParams& p, cudaStream_t stream, bool pdl) {
+template <int WN, int WK, bool kTwo>
+int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
+                        cudaStream_t stream, bool pdl) {
+  auto kern = w4a16_gemv_kernel<WN, WK, kTwo>;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) {
+      last_cuda_error() = static_cast<int>(e);
+      return TF_ERR_CUDA;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(plan.grid_x, plan.grid_y, plan.grid_z);
-  cfg.blockDim = dim3(32 * WN * WK);
-  cfg.dynamicSmemBytes = 0;
+  cfg.gridDim = dim3(plan.grid_x, plan.grid_y, 1);
+  cfg.blockDim = dim3(32 * kCtaWarps);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w4a16_mma_kernel<MT, WN, WK>, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
   if (e != cudaSuccess) {
     last_cuda_error() = static_cast<int>(e);
     return TF_ERR_CUDA;
@@ -272,21 +363,27 @@ int launch_variant(const LinearPlan& plan, const MmaParams& p, cudaStream_t stre
   return TF_OK;
 }
 
-template <int MT>
-int launch_mt(const LinearPlan& plan, const MmaParams& p, cudaStream_t stream, bool pdl) {
+template <bool kTwo>
+int launch_gemv_two(const LinearPlan& plan, const GemvParams& p, size_t smem, cudaStream_t st,
+                    bool pdl) {
   switch (plan.warps_k) {
-    case 1: return launch_variant<MT, 8, 1>(plan, p, stream, pdl);
-    case 2: return launch_variant<MT, 4, 2>(plan, p, stream, pdl);
-    case 4: return launch_variant<MT, 2, 4>(plan, p, stream, pdl);
-    case 8: return launch_variant<MT, 1, 8>(plan, p, stream, pdl);
+    case 1: return launch_gemv_variant<8, 1, kTwo>(plan, p, smem, st, pdl);
+    case 2: return launch_gemv_variant<4, 2, kTwo>(plan, p, smem, st, pdl);
+    case 4: return launch_gemv_variant<2, 4, kTwo>(plan, p, smem, st, pdl);
+    case 8: return launch_gemv_variant<1, 8, kTwo>(plan, p, smem, st, pdl);
     default: return TF_ERR_INVALID_ARG;
   }
 }
 
 }  // namespace
 
-int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream) {
-  MmaParams p;
+size_t gemv_smem_bytes(int64_t M, int bps) {
+  const int64_t stride = static_cast<int64_t>(bps) * kKB + 8;  // +16 B per row: bank offset
+  return static_cast<size_t>(M * stride * 2);
+}
+
+int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream) {
+  GemvParams p;
   p.x = reinterpret_cast<const __half*>(a.x);
   p.ldx = a.ldx;
   p.qw = a.qw;
@@ -296,18 +393,17 @@ int launch_mma_linear(const LinearPlan& plan, const LinearArgs& a, cudaStream_t 
   p.y = reinterpret_cast<__half*>(a.y);
   p.ldy = a.ldy;
   p.partial = plan.split_k > 1 ? static_cast<float*>(a.workspace) : nullptr;
-  p.M = a.M;
-  p.N = a.N;
-  p.K = a.K;
-  p.group_size = a.group_size;
+  p.M = static_cast<int>(a.M);
+  p.N = static_cast<int>(a.N);
+  p.K = static_cast<int>(a.K);
+  p.group_shift = a.group_size == 32 ? 5 : (a.group_size == 64 ? 6 : 7);
   p.split_k = plan.split_k;
-  p.blocks_per_split = plan.blocks_per_split;
-  const bool pdl = (launch_flags() & 1u) != 0;
-  int st;
-  if (plan.kernel == kKernelGemv)
-    st = launch_mt<1>(plan, p, stream, pdl);
-  else
-    st = launch_mt<8>(plan, p, stream, pdl);
+  p.bps = plan.blocks_per_split;
+  p.xs_stride = plan.blocks_per_split * kKB + 8;
+  const size_t smem = gemv_smem_bytes(a.M, plan.blocks_per_split);
+  const bool pdl = (launch_flags() & TF_LAUNCH_PDL) != 0;
+  const int st = a.group_size == 32 ? launch_gemv_two<true>(plan, p, smem, stream, pdl)
+                                    : launch_gemv_two<false>(plan, p, smem, stream, pdl);
   if (st != TF_OK || plan.split_k == 1) return st;
   return launch_splitk_reduce(p.partial, plan.split_k, a.M, a.N, a.bias, a.y, a.ldy, stream);
 }
