@@ -120,8 +120,9 @@ def test_entry_points_validate_before_touching_the_device() -> None:
     st = lib.tf_w4a16_linear(2, 1, 256, 256, 16, 16, 16, None, 64, 128, 16, 64, None, 0, None)
     assert st == _lib.TF_ERR_ALIGNMENT
     # A split-K launch without its workspace is refused.
-    assert workspace_bytes(1, 896, 4864, 128) > 0
-    st = lib.tf_w4a16_linear(16, 1, 4864, 4864, 16, 16, 16, None, 896, 128, 16, 896, None, 0, None)
+    assert launch_plan(8, 3584, 18944, 128).split_k > 1
+    st = lib.tf_w4a16_linear(16, 8, 18944, 18944, 16, 16, 16, None, 3584, 128, 16, 3584, None, 0,
+                             None)
     assert st == _lib.TF_ERR_WORKSPACE
     st = lib.tf_awq_repack(None, 12, 8, None, None)
     assert st == _lib.TF_ERR_INVALID_ARG
