@@ -11,15 +11,17 @@
 //     the warp one 16-byte shared load per packed word and no global address arithmetic;
 //   * a warp owns 16 weight rows and walks 256-wide K blocks; lane L = 4q + c loads 32 bytes of
 //     row n0+q and of row n0+q+8 (k in [256b + 64c, +64)), so each quad reads 128 contiguous bytes
-//     per row, and three blocks (weights, scales, zero points) are in flight per warp in a
-//     register ring, the first three requested before the programmatic-dependent-launch wait;
+//     per row, and three blocks (weights, scales, zero points) are held per warp in a register
+//     ring, the first three requested before the programmatic-dependent-launch wait;
 //   * rows beyond N and tokens beyond M are clamped for loading (never stored) instead of
 //     predicated; only a partial last K block takes predicated loads;
 //   * each packed word is unpacked with one shift: pairs 0 and 2 come from the mask 0x000F000F
 //     of w and w >> 8 (fp16 1024 + q), pairs 1 and 3 from the mask 0x00F000F0 (1024 + 16q), whose
 //     difference with 1024 + 16z is 16(q - z) exactly and is multiplied by the exact s/16, so both
 //     give the reference's correctly rounded fp16(q - z) * s. When a scale in the warp is too
-//     small for s/16 to be exact, the block takes the three-shift unpack instead (warp vote).
+//     small for s/16 to be exact (s/16 * 16 != s), the block takes the three-shift unpack instead
+//     (warp vote). Unpack and dequant are written in PTX (lop3, sub.rn / mul.rn.f16x2) so each
+//     pair costs exactly three instructions.
 // The dequantized pairs feed mma.m16n8k16 A fragments directly (the k order inside a step only
 // has to agree between A and B); the tensor core does the fp32 multiply-accumulate.
 // Warps that split K inside a CTA are summed through shared memory in warp order; CTAs that split
@@ -32,6 +34,7 @@ namespace {
 
 constexpr int kKB = 256;       // K values per block
 constexpr int kCtaWarps = 8;   // warps per CTA (WARPS_N x WARPS_K)
+constexpr int kPrefetch = 5;   // L2 prefetch distance in blocks (register loads run two ahead)
 
 struct GemvParams {
   const __half* x;
@@ -52,170 +55,200 @@ struct GemvParams {
 
 // One K block of a warp tile in registers: this lane's 64 values of k for two weight rows.
 struct GSlot {
-  uint4 wa0, wa1, wb0, wb1;      // rows A and B: words 0-3 and 4-7 of the lane's chunk
-  uint32_t s0, s1;               // scales (row A | row B << 16) of the chunk's two 32-k halves
-  uint32_t za0, zb0, za1, zb1;   // qzeros words of those halves
+  uint4 wa0, wa1, wb0, wb1;  // rows A and B: words 0-3 and 4-7 of the lane's chunk
+  uint32_t s0, s1;           // 32-bit words of the scales rows holding rows A and B's scales ...
+  uint32_t t0, t1;           // ... for the chunk's first and second 32-k half
+  uint32_t za0, zb0, za1, zb1;  // qzeros words of those halves
 };
 
 struct GLane {
-  const int32_t* wA;   // packed row A + this lane's word offset 8c
+  const int32_t* wA;    // packed row A + this lane's word offset 8c
   const int32_t* wB;
-  const __half* sA;    // scales + row A
-  const __half* sB;
-  const int32_t* zA;   // qzeros + row A / 8
+  const uint32_t* sA;   // the 32-bit word of the scales row that holds row A's scale
+  const uint32_t* sB;
+  const int32_t* zA;    // qzeros + row A / 8
   const int32_t* zB;
-  const uint4* xs;     // staged activations: token row q (clamped), + 64c
+  const uint4* xs;      // staged activations: token row q (clamped), + 64c
+  uint32_t s_sel;       // byte_perm selector: row A's scale (low half), row B's (high half)
   int nibA, nibB;
-  int kb0, b_end;      // this CTA's first block, this warp's end block (exclusive)
+  int kb0, b_end;       // this CTA's first block, this warp's end block (exclusive)
   int c;
 };
 
 __device__ __forceinline__ uint4 zero4() { return make_uint4(0, 0, 0, 0); }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// Ask L2 for block bb of this warp tile ahead of time (lane c == 0 of each quad fetches the
+// 128-byte lines of its rows A and B, quad 0 the scales and qzeros lines), so the register loads
+// issued one block ahead of use only wait for L2.
+__device__ __forceinline__ void gprefetch(int bb, const GemvParams& p, const GLane& L) {
+  if (bb >= L.b_end) return;
+  if (L.c == 0) {
+    prefetch_l2(L.wA + bb * (kKB / 8));
+    prefetch_l2(L.wB + bb * (kKB / 8));
+  }
+  if (threadIdx.x % 32 < 2) {  // lanes 0, 1: rows n0..n0+15 of the block's first group
+    const int g0 = (bb * kKB) >> p.group_shift;
+    if (threadIdx.x % 32 == 0)
+      prefetch_l2(L.sA + g0 * (p.N >> 1));
+    else
+      prefetch_l2(L.zA + g0 * (p.N >> 3));
+  }
+}
+
+// Register loads of block bb (halves past K read as zero weights, scale 0, zero point 0).
 template <bool kTwo>
 __device__ __forceinline__ void gload(GSlot& s, int bb, const GemvParams& p, const GLane& L) {
   if (bb >= L.b_end) return;  // warp-uniform: the slot is never consumed
-  const int wo = bb * (kKB / 8);
   const int k = bb * kKB + 64 * L.c;
   const int g0 = k >> p.group_shift;
-  const int n8 = p.N >> 3;
-  const uint4* pa = reinterpret_cast<const uint4*>(L.wA + wo);
-  const uint4* pb = reinterpret_cast<const uint4*>(L.wB + wo);
+  const int sw = p.N >> 1, n8 = p.N >> 3;
+  const uint4* pa = reinterpret_cast<const uint4*>(L.wA + bb * (kKB / 8));
+  const uint4* pb = reinterpret_cast<const uint4*>(L.wB + bb * (kKB / 8));
   if ((bb + 1) * kKB <= p.K) {
     s.wa0 = ldg_stream_v4(pa);
     s.wa1 = ldg_stream_v4(pa + 1);
     s.wb0 = ldg_stream_v4(pb);
     s.wb1 = ldg_stream_v4(pb + 1);
-    s.s0 = __half_as_ushort(__ldg(L.sA + g0 * p.N)) |
-           (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g0 * p.N))) << 16);
+    s.s0 = __ldg(L.sA + g0 * sw);
+    s.t0 = __ldg(L.sB + g0 * sw);
     s.za0 = static_cast<uint32_t>(__ldg(L.zA + g0 * n8));
     s.zb0 = static_cast<uint32_t>(__ldg(L.zB + g0 * n8));
     if constexpr (kTwo) {
-      const int g1 = g0 + 1;
-      s.s1 = __half_as_ushort(__ldg(L.sA + g1 * p.N)) |
-             (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g1 * p.N))) << 16);
-      s.za1 = static_cast<uint32_t>(__ldg(L.zA + g1 * n8));
-      s.zb1 = static_cast<uint32_t>(__ldg(L.zB + g1 * n8));
+      s.s1 = __ldg(L.sA + (g0 + 1) * sw);
+      s.t1 = __ldg(L.sB + (g0 + 1) * sw);
+      s.za1 = static_cast<uint32_t>(__ldg(L.zA + (g0 + 1) * n8));
+      s.zb1 = static_cast<uint32_t>(__ldg(L.zB + (g0 + 1) * n8));
     }
-  } else {  // partial last block: halves past K contribute exact zeros (s = 0, z = 0, q = 0)
+  } else {  // partial last block
     const bool in0 = k < p.K, in1 = k + 32 < p.K;
     s.wa0 = in0 ? ldg_stream_v4(pa) : zero4();
     s.wa1 = in1 ? ldg_stream_v4(pa + 1) : zero4();
     s.wb0 = in0 ? ldg_stream_v4(pb) : zero4();
     s.wb1 = in1 ? ldg_stream_v4(pb + 1) : zero4();
-    s.s0 = in0 ? (__half_as_ushort(__ldg(L.sA + g0 * p.N)) |
-                  (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g0 * p.N))) << 16))
-               : 0u;
+    s.s0 = in0 ? __ldg(L.sA + g0 * sw) : 0u;
+    s.t0 = in0 ? __ldg(L.sB + g0 * sw) : 0u;
     s.za0 = in0 ? static_cast<uint32_t>(__ldg(L.zA + g0 * n8)) : 0u;
     s.zb0 = in0 ? static_cast<uint32_t>(__ldg(L.zB + g0 * n8)) : 0u;
     if constexpr (kTwo) {
-      const int g1 = g0 + 1;
-      s.s1 = in1 ? (__half_as_ushort(__ldg(L.sA + g1 * p.N)) |
-                    (static_cast<uint32_t>(__half_as_ushort(__ldg(L.sB + g1 * p.N))) << 16))
-                 : 0u;
-      s.za1 = in1 ? static_cast<uint32_t>(__ldg(L.zA + g1 * n8)) : 0u;
-      s.zb1 = in1 ? static_cast<uint32_t>(__ldg(L.zB + g1 * n8)) : 0u;
-    } else if (!in1) {
-      // Group size >= 64: both halves share one group; a missing second half still needs s = 0.
-      s.s1 = 0u;
-      s.za1 = s.zb1 = 0u;
-    }
-  }
-  if constexpr (!kTwo) {
-    if ((bb + 1) * kKB <= p.K || k + 32 < p.K) {
-      s.s1 = s.s0;
-      s.za1 = s.za0;
-      s.zb1 = s.zb0;
+      s.s1 = in1 ? __ldg(L.sA + (g0 + 1) * sw) : 0u;
+      s.t1 = in1 ? __ldg(L.sB + (g0 + 1) * sw) : 0u;
+      s.za1 = in1 ? static_cast<uint32_t>(__ldg(L.zA + (g0 + 1) * n8)) : 0u;
+      s.zb1 = in1 ? static_cast<uint32_t>(__ldg(L.zB + (g0 + 1) * n8)) : 0u;
     }
   }
 }
 
-// A scale s admits the one-shift unpack iff s/16 is exact in fp16: zero, non-finite, or at
-// least 2^-10 in magnitude.
-__device__ __forceinline__ bool splits_exactly(uint32_t h) {
-  const uint32_t mag = h & 0x7FFFu;
-  return mag == 0u || mag >= 0x1400u;
+// PTX forms of the unpack and dequant, so each pair costs exactly one LOP3, one fp16x2 subtract
+// and one fp16x2 multiply (explicit .rn: never contracted into an FMA, which would round once
+// less than the reference).
+__device__ __forceinline__ uint32_t lop_mask_or(uint32_t w, uint32_t mask, uint32_t magic) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(magic));
+  return r;
 }
+__device__ __forceinline__ uint32_t hsub2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t dup_lo(uint32_t v) { return __byte_perm(v, v, 0x1010); }
+__device__ __forceinline__ uint32_t dup_hi(uint32_t v) { return __byte_perm(v, v, 0x3232); }
 
-__device__ __forceinline__ __half2 lo2(uint32_t s) {
-  const __half h = __ushort_as_half(static_cast<unsigned short>(s & 0xFFFFu));
-  return __halves2half2(h, h);
-}
-__device__ __forceinline__ __half2 hi2(uint32_t s) {
-  const __half h = __ushort_as_half(static_cast<unsigned short>(s >> 16));
-  return __halves2half2(h, h);
-}
+// Loop-invariant bit patterns, held in registers for the whole kernel.
+struct Consts {
+  uint32_t m1;     // 0x000F000F: pairs 0 and 2
+  uint32_t m16;    // 0x00F000F0: pairs 1 and 3 (value 16q)
+  uint32_t magic;  // 0x64006400: fp16 1024 in both halves
+};
 
 struct HalfConsts {  // per 32-k half of a chunk: zero-point magics and scales for rows A and B
-  __half2 z1A, z1B, z16A, z16B, s1A, s1B, s16A, s16B;
+  uint32_t z1A, z1B, z16A, z16B, s1A, s1B, s16A, s16B;
+  bool exact16;      // s/16 is exact for both rows (the one-shift unpack is valid)
 };
 
 __device__ __forceinline__ HalfConsts make_consts(uint32_t s, uint32_t za_w, uint32_t zb_w,
-                                                  const GLane& L) {
+                                                  const GLane& L, const Consts& C) {
   HalfConsts h;
   const uint32_t za = (za_w >> L.nibA) & 0xFu, zb = (zb_w >> L.nibB) & 0xFu;
-  h.z1A = zero_magic2(za);
-  h.z1B = zero_magic2(zb);
-  h.z16A = u32_as_h2(0x64006400u | (za << 4) | (za << 20));
-  h.z16B = u32_as_h2(0x64006400u | (zb << 4) | (zb << 20));
-  h.s1A = lo2(s);
-  h.s1B = hi2(s);
-  const __half2 sixteenth = __float2half2_rn(0.0625f);
-  h.s16A = __hmul2(h.s1A, sixteenth);
-  h.s16B = __hmul2(h.s1B, sixteenth);
+  h.z1A = (za * 0x00010001u) | C.magic;  // fp16 1024 + z in both halves
+  h.z1B = (zb * 0x00010001u) | C.magic;
+  h.z16A = (za * 0x00100010u) | C.magic;  // fp16 1024 + 16z
+  h.z16B = (zb * 0x00100010u) | C.magic;
+  const uint32_t s16 = hmul2_rn(s, 0x2C002C00u);  // s / 16 for rows A (low) and B (high)
+  // s/16 is exact iff multiplying it back by 16 returns s (false for NaN: exact path taken).
+  h.exact16 = hmul2_rn(s16, 0x4C004C00u) == s;
+  h.s1A = dup_lo(s);
+  h.s1B = dup_hi(s);
+  h.s16A = dup_lo(s16);
+  h.s16B = dup_hi(s16);
   return h;
 }
 
+// Pairs 0 and 2 are (w & 0x000F000F) and ((w >> 8) & 0x000F000F): fp16 1024 + q. Pairs 1 and 3
+// use the mask 0x00F000F0, giving 1024 + 16q: subtracting 1024 + 16z leaves 16(q - z) exactly,
+// and the exact s/16 turns it into the same correctly rounded fp16(q - z) * s as the reference.
 __device__ __forceinline__ void word_fast(float (&acc)[4], uint32_t wa, uint32_t wb,
-                                          const HalfConsts& h, const uint4& xv) {
+                                          const HalfConsts& h, const uint4& xv, const Consts& C) {
   const uint32_t a8 = wa >> 8, b8 = wb >> 8;
-  const uint32_t f0[4] = {dequant_pair((wa & 0x000F000Fu) | 0x64006400u, h.z1A, h.s1A),
-                          dequant_pair((wb & 0x000F000Fu) | 0x64006400u, h.z1B, h.s1B),
-                          dequant_pair((wa & 0x00F000F0u) | 0x64006400u, h.z16A, h.s16A),
-                          dequant_pair((wb & 0x00F000F0u) | 0x64006400u, h.z16B, h.s16B)};
-  const uint32_t f1[4] = {dequant_pair((a8 & 0x000F000Fu) | 0x64006400u, h.z1A, h.s1A),
-                          dequant_pair((b8 & 0x000F000Fu) | 0x64006400u, h.z1B, h.s1B),
-                          dequant_pair((a8 & 0x00F000F0u) | 0x64006400u, h.z16A, h.s16A),
-                          dequant_pair((b8 & 0x00F000F0u) | 0x64006400u, h.z16B, h.s16B)};
+  const uint32_t f0[4] = {hmul2_rn(hsub2_rn(lop_mask_or(wa, C.m1, C.magic), h.z1A), h.s1A),
+                          hmul2_rn(hsub2_rn(lop_mask_or(wb, C.m1, C.magic), h.z1B), h.s1B),
+                          hmul2_rn(hsub2_rn(lop_mask_or(wa, C.m16, C.magic), h.z16A), h.s16A),
+                          hmul2_rn(hsub2_rn(lop_mask_or(wb, C.m16, C.magic), h.z16B), h.s16B)};
+  const uint32_t f1[4] = {hmul2_rn(hsub2_rn(lop_mask_or(a8, C.m1, C.magic), h.z1A), h.s1A),
+                          hmul2_rn(hsub2_rn(lop_mask_or(b8, C.m1, C.magic), h.z1B), h.s1B),
+                          hmul2_rn(hsub2_rn(lop_mask_or(a8, C.m16, C.magic), h.z16A), h.s16A),
+                          hmul2_rn(hsub2_rn(lop_mask_or(b8, C.m16, C.magic), h.z16B), h.s16B)};
   mma_16816(acc, f0, xv.x, xv.y);
   mma_16816(acc, f1, xv.z, xv.w);
 }
 
+// Unit-scale unpack of every pair (three shifts per word): used for a block in which some scale
+// is too small for s/16 to be exact.
 __device__ __forceinline__ void word_exact(float (&acc)[4], uint32_t wa, uint32_t wb,
-                                           const HalfConsts& h, const uint4& xv) {
-  const uint32_t f0[4] = {dequant_pair(magic_pair(wa, 0), h.z1A, h.s1A),
-                          dequant_pair(magic_pair(wb, 0), h.z1B, h.s1B),
-                          dequant_pair(magic_pair(wa, 1), h.z1A, h.s1A),
-                          dequant_pair(magic_pair(wb, 1), h.z1B, h.s1B)};
-  const uint32_t f1[4] = {dequant_pair(magic_pair(wa, 2), h.z1A, h.s1A),
-                          dequant_pair(magic_pair(wb, 2), h.z1B, h.s1B),
-                          dequant_pair(magic_pair(wa, 3), h.z1A, h.s1A),
-                          dequant_pair(magic_pair(wb, 3), h.z1B, h.s1B)};
-  mma_16816(acc, f0, xv.x, xv.y);
-  mma_16816(acc, f1, xv.z, xv.w);
+                                           const HalfConsts& h, const uint4& xv, const Consts& C) {
+  uint32_t f[2][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t ma = lop_mask_or(wa >> (4 * j), C.m1, C.magic);
+    const uint32_t mb = lop_mask_or(wb >> (4 * j), C.m1, C.magic);
+    f[j >> 1][(j & 1) * 2 + 0] = hmul2_rn(hsub2_rn(ma, h.z1A), h.s1A);
+    f[j >> 1][(j & 1) * 2 + 1] = hmul2_rn(hsub2_rn(mb, h.z1B), h.s1B);
+  }
+  mma_16816(acc, f[0], xv.x, xv.y);
+  mma_16816(acc, f[1], xv.z, xv.w);
 }
 
 template <bool kTwo>
-__device__ __forceinline__ void gcompute(float (&acc)[4], const GSlot& s, int bb,
-                                         const GLane& L, int K) {
+__device__ __forceinline__ void gcompute(float (&acc)[2][4], const GSlot& s, int bb,
+                                         const GLane& L, int K, const Consts& C) {
   const uint4* xp = L.xs + (bb - L.kb0) * (kKB / 8);
-  const bool fast = __all_sync(0xffffffffu, splits_exactly(s.s0 & 0xFFFFu) &&
-                                                splits_exactly(s.s0 >> 16) &&
-                                                splits_exactly(s.s1 & 0xFFFFu) &&
-                                                splits_exactly(s.s1 >> 16));
-  // The second 32-k half has its own scale / zero point when the group size is 32, and in a
-  // partial last block (where a half past K carries s = 0, z = 0 so it adds exact zeros).
-  const bool partial = (bb + 1) * kKB > K;  // warp-uniform
-  const HalfConsts h0 = make_consts(s.s0, s.za0, s.zb0, L);
-  const HalfConsts h1 = (kTwo || partial) ? make_consts(s.s1, s.za1, s.zb1, L) : h0;
+  const HalfConsts h0 = make_consts(__byte_perm(s.s0, s.t0, L.s_sel), s.za0, s.zb0, L, C);
+  HalfConsts h1 = h0;
+  if constexpr (kTwo) {
+    h1 = make_consts(__byte_perm(s.s1, s.t1, L.s_sel), s.za1, s.zb1, L, C);
+  } else if ((bb + 1) * kKB > K) {  // warp-uniform: partial last block
+    // A second half past K has zero weights and zero activations; give it s = 0, z = 0 as well
+    // so it adds exact zeros whatever the first half's scale is.
+    if (bb * kKB + 64 * L.c + 32 >= K) h1 = make_consts(0u, 0u, 0u, L, C);
+  }
+  const bool fast = __all_sync(0xffffffffu, h0.exact16 && h1.exact16);
   const uint32_t wa[8] = {s.wa0.x, s.wa0.y, s.wa0.z, s.wa0.w, s.wa1.x, s.wa1.y, s.wa1.z, s.wa1.w};
   const uint32_t wb[8] = {s.wb0.x, s.wb0.y, s.wb0.z, s.wb0.w, s.wb1.x, s.wb1.y, s.wb1.z, s.wb1.w};
   if (fast) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) word_fast(acc, wa[j], wb[j], j < 4 ? h0 : h1, xp[j]);
+    for (int j = 0; j < 8; ++j) word_fast(acc[j & 1], wa[j], wb[j], j < 4 ? h0 : h1, xp[j], C);
   } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) word_exact(acc, wa[j], wb[j], j < 4 ? h0 : h1, xp[j]);
+    for (int j = 0; j < 8; ++j) word_exact(acc[j & 1], wa[j], wb[j], j < 4 ? h0 : h1, xp[j], C);
   }
 }
 
@@ -240,23 +273,31 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   const int64_t ldw = p.K / 8;
   L.wA = p.qw + ra * ldw + 8 * L.c;
   L.wB = p.qw + rb * ldw + 8 * L.c;
-  L.sA = p.scales + ra;
-  L.sB = p.scales + rb;
+  L.sA = reinterpret_cast<const uint32_t*>(p.scales) + (ra >> 1);
+  L.sB = reinterpret_cast<const uint32_t*>(p.scales) + (rb >> 1);
+  L.s_sel = ((ra & 1) ? 0x3232u : 0x1010u) & 0x00FFu;
+  L.s_sel |= ((rb & 1) ? 0x7676u : 0x5454u) & 0xFF00u;
   L.zA = p.qzeros + (ra >> 3);
   L.zB = p.qzeros + (rb >> 3);
   L.nibA = 4 * awq_nibble_of(ra & 7);
   L.nibB = 4 * awq_nibble_of(rb & 7);
   const int xq = min(q, p.M - 1);
   L.xs = xs_smem + (xq * p.xs_stride + 64 * L.c) / 8;
+  Consts C;
+  C.m1 = 0x000F000Fu;
+  C.m16 = 0x00F000F0u;
+  C.magic = 0x64006400u;
 
-  // Weights, scales and zero points of the first three blocks do not depend on the preceding
-  // kernel: request them before the programmatic-dependent-launch wait.
+  // Weights, scales and zero points never depend on the preceding kernel: the L2 prefetches of
+  // the first kPrefetch blocks and the register loads of the first two are issued before the
+  // programmatic-dependent-launch wait.
   const int b0 = L.kb0 + wk;
   constexpr int W = WARPS_K;
-  GSlot s0, s1, s2;
+#pragma unroll
+  for (int d = 2; d < kPrefetch; ++d) gprefetch(b0 + d * W, p, L);
+  GSlot s0, s1;
   gload<kTwo>(s0, b0, p, L);
   gload<kTwo>(s1, b0 + W, p, L);
-  gload<kTwo>(s2, b0 + 2 * W, p, L);
   pdl_wait();
 
   // Stage x[0:M, kb0*256 : kb1*256] (zero past K) in shared memory.
@@ -273,17 +314,21 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   }
   __syncthreads();
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int b = b0; b < L.b_end; b += 3 * W) {
-    gcompute<kTwo>(acc, s0, b, L, p.K);
-    gload<kTwo>(s0, b + 3 * W, p, L);
+  // Two accumulators (even / odd packed words) keep the tensor-core accumulate chains short;
+  // they are added in a fixed order at the end.
+  float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int b = b0; b < L.b_end; b += 2 * W) {
+    gprefetch(b + kPrefetch * W, p, L);
+    gcompute<kTwo>(acc2, s0, b, L, p.K, C);
+    gload<kTwo>(s0, b + 2 * W, p, L);
     if (b + W >= L.b_end) break;
-    gcompute<kTwo>(acc, s1, b + W, L, p.K);
-    gload<kTwo>(s1, b + 4 * W, p, L);
-    if (b + 2 * W >= L.b_end) break;
-    gcompute<kTwo>(acc, s2, b + 2 * W, L, p.K);
-    gload<kTwo>(s2, b + 5 * W, p, L);
+    gprefetch(b + (kPrefetch + 1) * W, p, L);
+    gcompute<kTwo>(acc2, s1, b + W, L, p.K, C);
+    gload<kTwo>(s1, b + 3 * W, p, L);
   }
+  float acc[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) acc[r] = acc2[0][r] + acc2[1][r];
   pdl_launch_dependents();
 
   if constexpr (WARPS_K > 1) {
@@ -400,10 +445,10 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   p.split_k = plan.split_k;
   p.bps = plan.blocks_per_split;
   p.xs_stride = plan.blocks_per_split * kKB + 8;
-  const size_t smem = gemv_smem_bytes(a.M, plan.blocks_per_split);
+  const size_t x_bytes = gemv_smem_bytes(a.M, plan.blocks_per_split);
   const bool pdl = (launch_flags() & TF_LAUNCH_PDL) != 0;
-  const int st = a.group_size == 32 ? launch_gemv_two<true>(plan, p, smem, stream, pdl)
-                                    : launch_gemv_two<false>(plan, p, smem, stream, pdl);
+  const int st = a.group_size == 32 ? launch_gemv_two<true>(plan, p, x_bytes, stream, pdl)
+                                    : launch_gemv_two<false>(plan, p, x_bytes, stream, pdl);
   if (st != TF_OK || plan.split_k == 1) return st;
   return launch_splitk_reduce(p.partial, plan.split_k, a.M, a.N, a.bias, a.y, a.ldy, stream);
 }
