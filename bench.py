@@ -179,9 +179,10 @@ class DecodeSweep:
                 self.calls.append((name, args))
         self.launches_per_step = 0
         for name, (nn, kk) in self.shard_shapes.items():
-            out = (ctypes.c_int32 * 8)()
+            out = (ctypes.c_int32 * 9)()
             self.lib.tf_launch_plan(m, nn, kk, G, ctypes.addressof(out))
-            self.launches_per_step += LAYERS * (1 + (1 if out[4] > 1 else 0))
+            outer_split = out[4] // max(out[8], 1)
+            self.launches_per_step += LAYERS * (1 + (1 if outer_split > 1 else 0))
 
     def step(self, only: str | None = None, allreduce: bool = True) -> None:
         import torch.distributed as dist

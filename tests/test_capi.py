@@ -69,14 +69,23 @@ def test_prefill_sizes_use_a_gemm(m: int) -> None:
 def test_plan_covers_every_k_block_once(n: int, k: int) -> None:
     plan = launch_plan(1, n, k, 128)
     assert plan.kernel == "gemv"
-    kblocks = -(-k // 256)  # the decode GEMV walks 256-wide K blocks
+    kblocks = -(-k // 128)  # the decode GEMV walks 128-wide K blocks
     assert plan.warps_k in (1, 2, 4, 8)
-    assert plan.grid_x * (8 // plan.warps_k) * 16 >= n
-    assert 1 <= plan.split_k <= 8
+    assert plan.cluster in (1, 2, 4, 8) and plan.split_k % plan.cluster == 0
+    assert plan.grid_x * (8 // plan.warps_k) * 32 >= n
     per = -(-kblocks // plan.split_k)
     assert (plan.split_k - 1) * per < kblocks <= plan.split_k * per  # no empty split
+    outer = plan.split_k // plan.cluster
     ws = workspace_bytes(1, n, k, 128)
-    assert ws >= (plan.split_k * n * 4 if plan.split_k > 1 else 0)
+    assert ws >= (outer * n * 4 if outer > 1 else 0)
+
+
+def test_decode_plan_fills_the_gpu_without_a_reduce_launch() -> None:
+    for n, k in [(4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944)]:
+        plan = launch_plan(1, n, k, 128)
+        ctas = plan.grid_x * plan.split_k
+        assert 148 <= ctas <= 296, (n, k, plan)
+        assert plan.split_k == plan.cluster  # any K split is reduced inside the cluster
 
 
 @pytest.mark.parametrize(("m", "n", "k"), [(1024, 3584, 18944), (64, 3584, 18944), (16, 37888, 3584)])
@@ -120,8 +129,9 @@ def test_entry_points_validate_before_touching_the_device() -> None:
     st = lib.tf_w4a16_linear(2, 1, 256, 256, 16, 16, 16, None, 64, 128, 16, 64, None, 0, None)
     assert st == _lib.TF_ERR_ALIGNMENT
     # A split-K launch without its workspace is refused.
-    assert launch_plan(8, 3584, 18944, 128).split_k > 1
-    st = lib.tf_w4a16_linear(16, 8, 18944, 18944, 16, 16, 16, None, 3584, 128, 16, 3584, None, 0,
+    plan = launch_plan(8, 65536, 65536, 128)
+    assert plan.split_k // plan.cluster > 1  # splits beyond one cluster need the workspace
+    st = lib.tf_w4a16_linear(16, 8, 65536, 65536, 16, 16, 16, None, 65536, 128, 16, 65536, None, 0,
                              None)
     assert st == _lib.TF_ERR_WORKSPACE
     st = lib.tf_awq_repack(None, 12, 8, None, None)

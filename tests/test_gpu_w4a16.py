@@ -90,16 +90,18 @@ def test_every_kernel_path(entry: str, g: int, m: int, with_bias: bool, device: 
 
 
 @pytest.mark.parametrize(("m", "n", "k"), [(8, 3584, 18944), (1, 1024, 16384), (3, 1024, 16384),
-                                           (1, 3584, 448 + 64), (2, 200, 4096)])
+                                           (1, 3584, 448 + 64), (2, 200, 4096), (8, 256, 65536)])
 def test_split_k_paths(m: int, n: int, k: int, device: torch.device) -> None:
-    """Shapes whose launch splits K across CTAs (fixed-order reduction of fp32 partials)."""
+    """Shapes whose launch splits K across CTAs: inside a cluster (partials summed through
+    distributed shared memory) and across clusters (fp32 partials + a reduce kernel)."""
     w = cases.layer_weights(n, k, 0)
     b = cases.bias(n, 0)
     x = cases.activations(m, k, 0)
     y = _linear(x.to(device), w.to(device), b.to(device))
     _check(y, x, w, b)
-    assert launch_plan(8, 3584, 18944, 128).split_k > 1
-    assert launch_plan(1, 1024, 16384, 128).split_k > 1
+    assert launch_plan(8, 3584, 18944, 128).cluster > 1
+    plan = launch_plan(8, 256, 65536, 128)
+    assert plan.split_k // plan.cluster > 1
 
 
 def test_leading_dims_and_bias_through_op(device: torch.device) -> None:

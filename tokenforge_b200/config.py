@@ -44,11 +44,12 @@ class LaunchPlan:
     tile_m: int
     grid_x: int
     grid_z: int
+    cluster: int
 
 
 def launch_plan(m: int, n: int, k: int, group_size: int) -> LaunchPlan:
     """The launch the kernel library will use for ``y[m, n] = x[m, k] W[n, k]^T``."""
-    out = (ctypes.c_int32 * 8)()
+    out = (ctypes.c_int32 * 9)()
     status = _lib.lib().tf_launch_plan(m, n, k, group_size, ctypes.addressof(out))
     if status != _lib.TF_OK:
         raise ValueError(
@@ -56,7 +57,7 @@ def launch_plan(m: int, n: int, k: int, group_size: int) -> LaunchPlan:
             f"{_lib.status_string(status)}"
         )
     v = list(out)
-    return LaunchPlan(KERNEL_NAMES[v[0]], v[1], v[2], v[3], v[4], v[5], v[6], v[7])
+    return LaunchPlan(KERNEL_NAMES[v[0]], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8])
 
 
 def workspace_bytes(m: int, n: int, k: int, group_size: int) -> int:

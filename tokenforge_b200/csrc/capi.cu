@@ -40,36 +40,53 @@ constexpr BucketEntry kTable[] = {
     {4096, kKernelTcGemm, 256}, {1 << 30, kKernelTcGemm, 256},
 };
 
-// Decode GEMV: 16-row warp tiles over 256-wide K blocks. Warps per tile (1..8) is the smallest
-// power of two that puts two CTAs' worth of warps on every SM, as long as each warp keeps at
-// least 1.5 blocks. K is split across CTAs (fp32 partials + a reduce launch) only when the tiles
-// cannot give every SM one CTA and each warp would still stream 8+ blocks, or when the staged
-// activations would not fit in 100 KB of shared memory.
+// Decode GEMV: 32-row warp tiles over 128-wide K blocks, K split over WARPS_K warps of a CTA and
+// over the C CTAs of a cluster. (WARPS_K, C) is the pair that brings the CTA count closest to two
+// per SM without exceeding it (ties: fewer warps per tile, then smaller clusters), keeping at least
+// one block per warp. C grows further if the CTA's staged activations would exceed 100 KB of
+// shared memory; beyond clusters of 8, K is also split across clusters (fp32 partials + reduce).
 int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   pl->tile_m = 8;
-  pl->tile_n = 16;
-  const int64_t n_tiles = cdiv(N, 16);
-  const int64_t kblocks = cdiv(K, 256);
-  int wk = 1;
-  while (wk < 8 && n_tiles * wk < 2 * 8 * kNumSms && 3 * (2 * wk) <= 2 * kblocks) wk *= 2;
-  pl->warps_k = wk;
-  const int64_t gx = cdiv(n_tiles, 8 / wk);
-  int64_t split = 1;
-  if (n_tiles * wk < 8 * kNumSms && kblocks >= 8 * wk) {
-    split = std::min<int64_t>(8, cdiv(2 * 8 * kNumSms, n_tiles * wk));
-    split = std::max<int64_t>(1, std::min<int64_t>(split, kblocks / (4 * wk)));
+  pl->tile_n = 32;
+  const int64_t n_tiles = cdiv(N, 32);
+  const int64_t kblocks = cdiv(K, 128);
+  const int64_t target = 2 * kNumSms;
+  int best_wk = 1, best_c = 1;
+  int64_t best_ctas = -1;
+  for (int c = 1; c <= 8; c *= 2) {
+    for (int wk = 1; wk <= 8; wk *= 2) {
+      if (static_cast<int64_t>(wk) * c > kblocks && !(wk == 1 && c == 1)) continue;
+      const int64_t ctas = cdiv(n_tiles, 8 / wk) * c;
+      if (ctas > target && !(wk == 1 && c == 1)) continue;
+      const bool better = ctas > best_ctas ||
+                          (ctas == best_ctas && static_cast<int64_t>(wk) * c <
+                                                    static_cast<int64_t>(best_wk) * best_c);
+      if (better) {
+        best_ctas = ctas;
+        best_wk = wk;
+        best_c = c;
+      }
+    }
   }
-  const int64_t max_bps = std::max<int64_t>(1, ((100 * 1024) / (2 * M) - 8) / 256);
-  split = std::max<int64_t>(split, cdiv(kblocks, max_bps));
-  const int64_t per = cdiv(kblocks, split);
-  split = cdiv(kblocks, per);
-  if (gx > 0x7fffffffLL || split > 65535) return TF_ERR_UNSUPPORTED;
-  pl->split_k = static_cast<int>(split);
+  // Shared-memory bound on the staged activations: M x (K / splits) fp16 <= 100 KB.
+  int64_t splits = best_c;
+  auto x_bytes = [&](int64_t sp) { return 2 * M * (cdiv(kblocks, sp) * 128 + 8); };
+  while (x_bytes(splits) > 100 * 1024 && splits < kblocks) splits *= 2;
+  int cluster = static_cast<int>(std::min<int64_t>(splits, 8));
+  const int64_t per = cdiv(kblocks, splits);
+  splits = cdiv(kblocks, per);
+  if (splits % cluster != 0) splits = cdiv(splits, cluster) * cluster;  // whole clusters
+  const int64_t gx = cdiv(n_tiles, 8 / best_wk);
+  if (gx > 0x7fffffffLL || splits > 65535) return TF_ERR_UNSUPPORTED;
+  pl->warps_k = best_wk;
+  pl->cluster = cluster;
+  pl->split_k = static_cast<int>(splits);
   pl->blocks_per_split = static_cast<int>(per);
   pl->grid_x = static_cast<unsigned>(gx);
-  pl->grid_y = static_cast<unsigned>(split);
+  pl->grid_y = static_cast<unsigned>(splits);
   pl->grid_z = 1;
-  pl->workspace = split > 1 ? static_cast<size_t>(split * M * N) * sizeof(float) : 0;
+  const int64_t outer = splits / cluster;
+  pl->workspace = outer > 1 ? static_cast<size_t>(outer * M * N) * sizeof(float) : 0;
   return TF_OK;
 }
 
@@ -96,6 +113,7 @@ int plan_mma(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   split = cdiv(kblocks, per);
   if (gx > 0x7fffffffLL || gz > 65535 || split > 65535) return TF_ERR_UNSUPPORTED;
   pl->split_k = static_cast<int>(split);
+  pl->cluster = 1;
   pl->blocks_per_split = static_cast<int>(per);
   pl->grid_x = static_cast<unsigned>(gx);
   pl->grid_y = static_cast<unsigned>(split);
@@ -258,6 +276,7 @@ int tf_launch_plan(int64_t M, int64_t N, int64_t K, int32_t group_size, int32_t*
   out[5] = pl.tile_m;
   out[6] = static_cast<int32_t>(pl.grid_x);
   out[7] = static_cast<int32_t>(pl.grid_z);
+  out[8] = pl.cluster;
   return TF_OK;
 }
 

@@ -19,6 +19,7 @@ struct LinearPlan {
   int tile_n;            // weight rows per warp tile (mma) or per CTA tile (tcgen05)
   int warps_k;           // warps splitting K inside one CTA (mma kernels)
   int split_k;           // CTAs splitting K (partials reduced in a fixed order)
+  int cluster;           // of those, CTAs per thread-block cluster (reduced through DSMEM)
   int tile_m;            // tokens per CTA tile
   int blocks_per_split;  // K blocks per split: 256 wide (GEMV), 128 (MMA tiles), 64 (tcgen05)
   unsigned grid_x, grid_y, grid_z;
@@ -48,7 +49,7 @@ struct LinearArgs {
 
 int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 int launch_mma_tiles(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
-// Dynamic shared memory of the decode GEMV: M staged activation rows of bps * 256 (+8) fp16.
+// Dynamic shared memory of the decode GEMV: M staged activation rows of bps * 128 (+8) fp16.
 size_t gemv_smem_bytes(int64_t M, int bps);
 int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size);

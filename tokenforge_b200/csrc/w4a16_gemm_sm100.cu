@@ -605,6 +605,7 @@ void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   }
   const int64_t per = cdiv(kb, best_s);
   pl->split_k = static_cast<int>(cdiv(kb, per));
+  pl->cluster = 1;
   pl->blocks_per_split = static_cast<int>(per);
   pl->tile_n = kBlockN;
   pl->warps_k = 1;
