@@ -11,12 +11,13 @@
 //     contiguous rows 4q..4q+3 (tile 0 rows q / q+8 <- rows 4q / 4q+1, tile 1 <- 4q+2 / 4q+3), so
 //     their four scales arrive in one 8-byte load already paired the way the fragments use them,
 //     their zero points sit in one qzeros word, and one activation fragment feeds both tiles;
-//   * the warp walks 128-wide K blocks; lane c reads 16 bytes (k in [128b + 32c, +32)) of each of
-//     its rows, so a quad reads 64 contiguous bytes per row;
+//   * the warp walks a contiguous range of 128-wide K blocks; lane c reads 16 bytes (k in
+//     [128b + 32c, +32)) of each of its rows, so a quad reads 64 contiguous bytes per row;
 //   * the CTA's activations x[0:M, k-range] are staged once in shared memory;
 //   * weights, scales and zero points are loaded into registers two blocks ahead, and requested
-//     from L2 kPrefetch blocks ahead (prefetch.global.L2), so register loads only wait for L2;
-//     the first loads are issued before the programmatic-dependent-launch wait;
+//     from L2 kPrefetch blocks ahead, four blocks (256 bytes per row) per bulk prefetch, so the
+//     register loads only wait for L2; the first loads are issued before the
+//     programmatic-dependent-launch wait;
 //   * rows beyond N and tokens beyond M are clamped for loading (never stored); only a partial
 //     last K block takes predicated loads;
 //   * unpack and dequant are PTX (lop3, sub.rn / mul.rn.f16x2): exactly three instructions per
@@ -37,7 +38,7 @@ namespace {
 constexpr int kKB = 128;         // K values per block
 constexpr int kCtaWarps = 8;     // warps per CTA (WARPS_N x WARPS_K)
 constexpr int kWarpRows = 32;    // weight rows per warp tile
-constexpr int kPrefetch = 6;     // L2 prefetch distance in blocks
+constexpr int kPrefetch = 8;     // L2 prefetch distance in blocks (issued four blocks at a time)
 
 struct GemvParams {
   const __half* x;
@@ -80,19 +81,26 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-// L2 prefetch of block bb: lane c == 0 of each quad asks for the 64-byte row segments of its four
-// rows, lane 0 for the block's scales and qzeros lines.
-__device__ __forceinline__ void gprefetch(int bb, const GemvParams& p, const GLane& L) {
-  if (bb >= L.b_end) return;
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// L2 prefetch of blocks [bb, bb + nb) of this warp's rows: lane c == 0 of each quad asks for the
+// nb * 64 contiguous bytes of each of its four rows (one bulk prefetch per row), lane 0 for the
+// scales and qzeros lines of those blocks' groups.
+__device__ __forceinline__ void gprefetch(int bb, int nb, const GemvParams& p, const GLane& L) {
+  if (nb <= 0) return;
   if (L.c == 0) {
-    const int32_t* r = L.w + bb * (kKB / 8);
+    const int32_t* r = L.w + bb * (kKB / 8);  // c == 0: the row's segment starts here
 #pragma unroll
-    for (int j = 0; j < 4; ++j) prefetch_l2(r + j * L.ldw);
+    for (int j = 0; j < 4; ++j) bulk_prefetch_l2(r + j * L.ldw, static_cast<uint32_t>(nb) * 64u);
   }
   if ((threadIdx.x & 31) == 0) {
-    const int g = (bb * kKB) >> p.group_shift;
-    prefetch_l2(L.s + g * (p.N >> 2));
-    prefetch_l2(L.z + g * (p.N >> 3));
+    for (int t = 0; t < nb; ++t) {
+      const int g = ((bb + t) * kKB) >> p.group_shift;
+      prefetch_l2(L.s + g * (p.N >> 2));
+      prefetch_l2(L.z + g * (p.N >> 3));
+    }
   }
 }
 
@@ -213,7 +221,10 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   const int nblk = (p.K + kKB - 1) / kKB;
   L.kb0 = blockIdx.y * p.bps;
   const int kb1 = min(nblk, L.kb0 + p.bps);
-  L.b_end = kb1;
+  // Warp wk of a row group takes a contiguous share of the CTA's K blocks.
+  const int share = (kb1 - L.kb0 + WARPS_K - 1) / WARPS_K;
+  const int b0 = L.kb0 + wk * share;
+  L.b_end = min(kb1, b0 + share);
   L.ldw = p.K / 8;
   L.w = p.qw + r0 * L.ldw + 4 * L.c;
   L.s = reinterpret_cast<const uint2*>(p.scales + r0);
@@ -227,13 +238,10 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   // Weights, scales and zero points never depend on the preceding kernel: the L2 prefetches of
   // the first blocks and the register loads of the first two are issued before the
   // programmatic-dependent-launch wait.
-  const int b0 = L.kb0 + wk;
-  constexpr int W = WARPS_K;
-#pragma unroll
-  for (int d = 2; d < kPrefetch; ++d) gprefetch(b0 + d * W, p, L);
+  gprefetch(b0 + 2, min(b0 + 2 + kPrefetch, L.b_end) - (b0 + 2), p, L);
   GSlot s0, s1;
   gload(s0, b0, p, L);
-  gload(s1, b0 + W, p, L);
+  gload(s1, b0 + 1, p, L);
   pdl_wait();
 
   // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory.
@@ -251,14 +259,16 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   __syncthreads();
 
   float acc[2][2][4] = {};
-  for (int b = b0; b < L.b_end; b += 2 * W) {
-    gprefetch(b + kPrefetch * W, p, L);
+  for (int b = b0; b < L.b_end; b += 2) {
+    if (((b - b0) & 3) == 2) {  // every fourth block: the four blocks kPrefetch ahead
+      const int pb = b + kPrefetch;
+      gprefetch(pb, min(4, L.b_end - pb), p, L);
+    }
     gcompute(acc, s0, b, L, mask, magic);
-    gload(s0, b + 2 * W, p, L);
-    if (b + W >= L.b_end) break;
-    gprefetch(b + (kPrefetch + 1) * W, p, L);
-    gcompute(acc, s1, b + W, L, mask, magic);
-    gload(s1, b + 3 * W, p, L);
+    gload(s0, b + 2, p, L);
+    if (b + 1 >= L.b_end) break;
+    gcompute(acc, s1, b + 1, L, mask, magic);
+    gload(s1, b + 3, p, L);
   }
   pdl_launch_dependents();
 
