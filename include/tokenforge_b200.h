@@ -135,6 +135,27 @@ TF_API int tf_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
                     uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* tf_w4a16_linear with no workspace argument: the split-K partials go to a fixed buffer the
+ * library holds in device memory (a static __device__ array of TF_NOALLOC_SCRATCH_BYTES per
+ * device). No counterpart in the reference. It is for callers that cannot allocate device memory
+ * at the call site: a C/C++ engine that plans all its memory before serving and owns no
+ * allocator at launch time, or a host without torch to hand out a workspace.
+ * - Launches, output and error statuses are those of tf_w4a16_linear (same plan, same kernels).
+ * - A shape whose plan needs more than TF_NOALLOC_SCRATCH_BYTES of partials (large prefill M
+ *   with split K) returns TF_ERR_TOO_LARGE without launching; use tf_w4a16_linear for it.
+ * - The first call on each device (current device) looks the buffer up once
+ *   (cudaGetSymbolAddress, which may load the library's kernels); make that first call before
+ *   any stream capture.
+ * - The buffer needs no clearing: each split writes its whole slice before it is read.
+ * - One buffer per device: calls that can overlap on the device (several streams, several host
+ *   threads) race on it. Issue them on one stream, or use tf_w4a16_linear with a workspace
+ *   each. */
+#define TF_NOALLOC_SCRATCH_BYTES (16u << 20)
+TF_API int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                    const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                    const uint16_t* bias, int64_t N, int32_t group_size,
+                    uint16_t* y, int64_t ldy, void* stream);
+
 /* Launch-table introspection (replaces config.default_config / GemmConfig, config.py:23-92).
  * Writes the launch chosen for (M, N, K, G) into out[0..8]:
  *   {kernel (0 = gemv, 1 = mma gemm, 2 = tcgen05 gemm), m_bucket, tile_n, warps_k, split_k,

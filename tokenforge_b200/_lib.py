@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _SZ, _P],
     ),
+    "tf_w4a16_linear_noalloc": (
+        ctypes.c_int,
+        [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P],
+    ),
     "tf_launch_plan": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P]),
     "tf_rmsnorm_fp8_quant": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _F32, _P, _P, _P, _P]),
     "tf_cast_e4m3": (ctypes.c_int, [_P, _I64, _P, _P]),

@@ -7,6 +7,7 @@
 // given (M, N, K, G) always launches the same grid and produces bit-identical output.
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "tf_common.cuh"
 #include "tf_plan.h"
@@ -220,8 +221,48 @@ LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const
   return a;
 }
 
+// Fixed scratch of tf_w4a16_linear_noalloc. Callers of that entry point own no allocator at the
+// call site (an engine that sized all of its device memory up front, or C code without torch), so
+// the split-K partials live in this array, which the module loader places in device memory with
+// the kernels. 16 MiB covers every decode plan and prefill plans up to a few hundred tokens at
+// the benchmark's widths; larger plans are refused, not truncated.
+constexpr size_t kNoallocScratchBytes = 16u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch on the current device, looked up once per device.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    last_cuda_error() = static_cast<int>(e);
+    return TF_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return TF_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      last_cuda_error() = static_cast<int>(e);
+      return TF_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return TF_OK;
+}
+
 }  // namespace
 }  // namespace tfb
+
+static_assert(tfb::kNoallocScratchBytes == TF_NOALLOC_SCRATCH_BYTES,
+              "header and library disagree on the fixed scratch size");
 
 extern "C" {
 
@@ -305,6 +346,24 @@ int tf_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
   const auto a = tfb::make_args(x, M, K, ldx, qweight_t, scales, qzeros, bias, N, group_size, y,
                                 ldy, workspace, workspace_bytes);
   return tfb::run_linear(a, static_cast<cudaStream_t>(stream), -1);
+}
+
+int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                            const int32_t* qweight_t, const uint16_t* scales,
+                            const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                            int32_t group_size, uint16_t* y, int64_t ldy, void* stream) {
+  auto a = tfb::make_args(x, M, K, ldx, qweight_t, scales, qzeros, bias, N, group_size, y, ldy,
+                          nullptr, 0);
+  int st = tfb::validate_linear(a);
+  if (st != TF_OK || M == 0) return st;
+  void* scratch = nullptr;
+  st = tfb::noalloc_scratch(&scratch);
+  if (st != TF_OK) return st;
+  a.workspace = scratch;
+  a.workspace_bytes = tfb::kNoallocScratchBytes;
+  st = tfb::run_linear(a, static_cast<cudaStream_t>(stream), -1);
+  // The scratch is never null here, so a workspace refusal means the plan outgrew it.
+  return st == TF_ERR_WORKSPACE ? TF_ERR_TOO_LARGE : st;
 }
 
 }  // extern "C"
