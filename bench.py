@@ -53,6 +53,26 @@ def algorithmic_bytes(m: int, n: int, k: int, g: int = G) -> int:
     return n * k // 2 + (k // g) * n * 2 + (k // g) * n // 2 + m * k * 2 + m * n * 2
 
 
+def metric_name(m: int) -> str:
+    return f"W4A16 GEMV HBM GB/s at M={m} (Qwen2.5-7B decode sweep, 28 layers)"
+
+
+TRAFFIC_FILE = ROOT / "profiles" / "w4a16_gemv_decode_dram.json"
+
+
+def dram_traffic(kinds: list[str], n_layers: int, m: int, world: int) -> dict | None:
+    """DRAM bytes (read + write) per launch of each layer type, from the committed ncu capture
+    (dram__bytes_read.sum + dram__bytes_write.sum), scaled to one step of this sweep."""
+    if not TRAFFIC_FILE.exists():
+        return None
+    d = json.loads(TRAFFIC_FILE.read_text())
+    per = d.get("dram_bytes_per_launch", {})
+    if d.get("m") != m or d.get("tp") != world or any(k not in per for k in kinds):
+        return None
+    return {"bytes_per_step": int(sum(per[k] for k in kinds) * n_layers),
+            "per_launch": {k: per[k] for k in kinds}}
+
+
 def peaks() -> tuple[dict[str, float], str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -65,31 +85,40 @@ def peaks() -> tuple[dict[str, float], str]:
 
 
 class ClockSampler:
-    """Samples SM clock and throttle reasons with nvidia-smi while the timed region runs."""
+    """Samples SM clock and throttle reasons with nvidia-smi while the GPU is under load.
+
+    Polls every ~50 ms from a background thread. :meth:`window` brackets the timed region; the
+    summary reports the samples taken inside it, and when the region is shorter than one poll,
+    the samples of the untimed settle phase that runs the same graph immediately before it
+    (``"window"`` says which).
+    """
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, index: int) -> None:
         self.index = index
-        self.samples: list[list[str]] = []
+        self.samples: list[tuple[float, list[str]]] = []  # (host time at the poll's midpoint, fields)
+        self.t0 = self.t1 = 0.0
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
 
     def _run(self) -> None:
         while not self._stop.is_set():
+            t = time.monotonic()
             try:
                 out = subprocess.run(
                     ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                      "--format=csv,noheader,nounits"],
                     capture_output=True, text=True, timeout=5,
                 ).stdout.strip()
-                if out:
-                    self.samples.append([v.strip() for v in out.split(",")])
             except (OSError, subprocess.SubprocessError):
                 return
-            self._stop.wait(0.2)
+            if out:
+                self.samples.append((0.5 * (t + time.monotonic()), [v.strip() for v in out.split(",")]))
+            self._stop.wait(0.05)
 
     def __enter__(self) -> ClockSampler:
         self._thread.start()
@@ -99,19 +128,39 @@ class ClockSampler:
         self._stop.set()
         self._thread.join(timeout=10)
 
+    def window(self, start: bool) -> None:
+        if start:
+            self.t0 = time.monotonic()
+        else:
+            self.t1 = time.monotonic()
+
     def summary(self) -> dict[str, object]:
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
-        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4)
-                          if len(s) > 3 + i and s[3 + i].lower() == "active"})
+        inside = [f for t, f in self.samples if self.t0 <= t <= self.t1]
+        where = "timed region"
+        if not inside:
+            inside = [f for t, f in self.samples if t <= self.t1]
+            where = "settle phase before the timed region (same graph) + timed region"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(v: str) -> float | None:
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [x for x in (num(f[0]) for f in inside) if x is not None]
+        mx = [x for x in (num(f[1]) for f in inside) if x is not None]
+        pw = [x for x in (num(f[2]) for f in inside) if x is not None]
+        reasons = sorted({self.NAMES[i] for f in inside for i in range(4)
+                          if len(f) > 3 + i and f[3 + i].lower() == "active"})
         return {
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(mx) if mx else None,
+            "power_w": round(statistics.median(pw), 1) if pw else None,
             "reasons": reasons,
-            "samples": len(self.samples),
+            "samples": len(inside),
+            "window": where,
         }
 
 
@@ -121,19 +170,23 @@ class ClockSampler:
 class DecodeSweep:
     """This rank's shards of the 28-layer sweep plus the C-ABI argument tuples of a step."""
 
-    def __init__(self, m: int, rank: int, world: int, device: torch.device, seed: int = 0) -> None:
+    def __init__(self, m: int, rank: int, world: int, device: torch.device, seed: int = 0,
+                 kinds: tuple[str, ...] | None = None, n_layers: int = LAYERS) -> None:
         from tokenforge_b200 import _lib, tp
         from tokenforge_b200.pack import W4A16Weights
 
         self.m, self.rank, self.world, self.device = m, rank, world, device
+        self.n_layers = n_layers
+        shapes = [s for s in LAYER_SHAPES if kinds is None or s[0] in kinds]
+        self.kinds = [s[0] for s in shapes]
         self.lib = _lib.lib()
         gen = torch.Generator(device=device).manual_seed(seed * 7919 + rank)
         self.layers: list[list[tuple[str, W4A16Weights, tuple[int, int]]]] = []
         self.bytes_per_step = 0  # this rank's algorithmic bytes
         self.shard_shapes: dict[str, tuple[int, int]] = {}
-        for _ in range(LAYERS):
+        for _ in range(n_layers):
             row = []
-            for name, n, k, kind in LAYER_SHAPES:
+            for name, n, k, kind in shapes:
                 if kind == "column":
                     n0, n1 = tp.column_bounds(n, world)[rank]
                     nn, kk, bounds = n1 - n0, k, (n0, n1)
@@ -157,7 +210,7 @@ class DecodeSweep:
         self.x_o = torch.randn((m, HIDDEN), generator=xg, device=device).to(torch.float16)
         self.x_d = torch.randn((m, INTER), generator=xg, device=device).to(torch.float16)
         self.y = {name: torch.empty((m, self.shard_shapes[name][0]), dtype=torch.float16,
-                                    device=device) for name, *_ in LAYER_SHAPES}
+                                    device=device) for name in self.kinds}
         ws = max(int(self.lib.tf_w4a16_workspace_bytes(m, nn, kk, G))
                  for nn, kk in self.shard_shapes.values())
         self.ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=device)
@@ -182,7 +235,7 @@ class DecodeSweep:
             out = (ctypes.c_int32 * 9)()
             self.lib.tf_launch_plan(m, nn, kk, G, ctypes.addressof(out))
             outer_split = out[4] // max(out[8], 1)
-            self.launches_per_step += LAYERS * (1 + (1 if outer_split > 1 else 0))
+            self.launches_per_step += n_layers * (1 + (1 if outer_split > 1 else 0))
 
     def step(self, only: str | None = None, allreduce: bool = True) -> None:
         import torch.distributed as dist
@@ -213,52 +266,77 @@ def capture(fn, device: torch.device) -> torch.cuda.CUDAGraph:  # type: ignore[n
     return g
 
 
-def time_graph(g: torch.cuda.CUDAGraph, reps: int, device: torch.device, barrier=None) -> float:  # type: ignore[no-untyped-def]
-    """Milliseconds for ``reps`` back-to-back replays, timed with CUDA events."""
+def time_graph(g: torch.cuda.CUDAGraph, reps: int, device: torch.device, barrier=None,  # type: ignore[no-untyped-def]
+               clocks: ClockSampler | None = None) -> float:
+    """Milliseconds for ``reps`` back-to-back replays, timed with CUDA events on the current
+    stream (the one the graph is replayed on), with a synchronize (and barrier) on both sides."""
     torch.cuda.synchronize(device)
     if barrier:
         barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.window(True)
     start.record()
     for _ in range(reps):
         g.replay()
     end.record()
     torch.cuda.synchronize(device)
+    if clocks:
+        clocks.window(False)
+    if barrier:
+        barrier()
     return start.elapsed_time(end)
 
 
 # ----------------------------------------------------------------------------- CPU baseline
 
 
-def cpu_baseline(m: int, reps: int = 1) -> dict[str, object]:
-    """The oracle's C port of the reference CPU path on one decoder layer (all host cores)."""
-    from oracle import oracle
+class CpuLayerSample:
+    """One decoder layer (qkv, o, gate_up, down) at M tokens for the oracle's C port of the
+    reference CPU path (dequantize + fp32 matmul, all host cores)."""
 
-    cores = os.cpu_count() or 1
-    gen = torch.Generator().manual_seed(5)
-    tensors, total = [], 0
-    for _, n, k, _ in LAYER_SHAPES:
-        qw = torch.randint(-(2**31), 2**31 - 1, (n, k // 8), generator=gen, dtype=torch.int32)
-        z = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32)
-        s = (torch.rand((k // G, n), generator=gen) * 0.018 + 0.002).to(torch.float16)
-        x = torch.randn((m, k), generator=gen).to(torch.float16)
-        tensors.append((x, qw, s, z))
-        total += algorithmic_bytes(m, n, k)
-    times = []
-    for _ in range(reps):
+    def __init__(self, m: int) -> None:
+        self.m = m
+        self.cores = os.cpu_count() or 1
+        gen = torch.Generator().manual_seed(5)
+        self.tensors, self.bytes = [], 0
+        for _, n, k, _ in LAYER_SHAPES:
+            qw = torch.randint(-(2**31), 2**31 - 1, (n, k // 8), generator=gen, dtype=torch.int32)
+            z = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32)
+            s = (torch.rand((k // G, n), generator=gen) * 0.018 + 0.002).to(torch.float16)
+            x = torch.randn((m, k), generator=gen).to(torch.float16)
+            self.tensors.append((x, qw, s, z))
+            self.bytes += algorithmic_bytes(m, n, k)
+
+    def run(self) -> float:
+        """Seconds for one pass over the layer."""
+        from oracle import oracle
+
         t0 = time.perf_counter()
-        for x, qw, s, z in tensors:
-            oracle.w4a16_cpu(x, qw, s, z, G, threads=cores)
-        times.append(time.perf_counter() - t0)
+        for x, qw, s, z in self.tensors:
+            oracle.w4a16_cpu(x, qw, s, z, G, threads=self.cores)
+        return time.perf_counter() - t0
+
+    def describe(self, reps: int) -> str:
+        return (f"one decoder layer (qkv, o, gate_up, down) at M={self.m}, {self.bytes} algorithmic "
+                f"bytes per pass, median of {reps} passes")
+
+
+def cpu_baseline(m: int, min_seconds: float = 10.0) -> dict[str, object]:
+    """The CPU port timed for about ``min_seconds`` (at least 3 passes), median pass."""
+    sample = CpuLayerSample(m)
+    sample.run()  # first touch of the inputs
+    times: list[float] = []
+    while len(times) < 3 or sum(times) < min_seconds:
+        times.append(sample.run())
     sec = statistics.median(times)
     return {
-        "value": round(total / sec / 1e9, 4),
+        "value": round(sample.bytes / sec / 1e9, 4),
         "unit": "GB/s",
-        "cores": cores,
+        "cores": sample.cores,
         "kind": "port",
-        "sample": f"one decoder layer (qkv, o, gate_up, down) at M={m}, {total} algorithmic "
-                  f"bytes, median of {reps}",
+        "sample": sample.describe(len(times)),
         "seconds_per_sample": round(sec, 4),
     }
 
@@ -268,17 +346,17 @@ def run_reference(args: argparse.Namespace) -> None:
     if rank != 0:
         return
     t_all = time.perf_counter()
+    sample = CpuLayerSample(args.m)
     for _ in range(args.warmup):
-        cpu_baseline(args.m, reps=1)
-    samples = [cpu_baseline(args.m, reps=1) for _ in range(args.steps)]
-    value = statistics.median(float(s["value"]) for s in samples)
-    sec = statistics.median(float(s["seconds_per_sample"]) for s in samples)
-    cb = dict(samples[0])
-    cb["value"] = value
-    cb.pop("seconds_per_sample", None)
+        sample.run()
+    times = [sample.run() for _ in range(args.steps)]
+    sec = statistics.median(times)
+    value = round(sample.bytes / sec / 1e9, 4)
+    cb = {"value": value, "unit": "GB/s", "cores": sample.cores, "kind": "port",
+          "sample": sample.describe(len(times))}
     line = {
         "impl": "reference",
-        "metric": "W4A16 GEMV HBM GB/s at M=1 (Qwen2.5-7B decode sweep)",
+        "metric": metric_name(args.m),
         "value": value,
         "unit": "GB/s",
         "n_gpus": args.gpus,
@@ -290,7 +368,8 @@ def run_reference(args: argparse.Namespace) -> None:
         "vs_baseline": None,
         "dtype": "int4xfp16->fp32",
         "data": "synthetic",
-        "config": {"workload": f"config3 decode sweep sample: one decoder layer at M={args.m}",
+        "config": {"workload": f"config3 decode sweep: 28 layers x (qkv, o, gate_up, down), "
+                               f"M={args.m}; each step times one of its decoder layers on the CPU",
                    "m": args.m, "group_size": G},
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -363,6 +442,10 @@ def main() -> None:
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
+    ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
+                    help="restrict the sweep to these layer types (profiling a small case)")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers in the sweep (28 = Qwen2.5-7B; fewer for a small case)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warmup must be >= 3", file=sys.stderr)
@@ -388,7 +471,9 @@ def main() -> None:
     _lib.set_launch_flags(0 if args.no_pdl else _lib.TF_LAUNCH_PDL)
     pk, src = peaks()
 
-    sweep = DecodeSweep(args.m, rank, world, device)
+    full = args.layer is None and args.layers == LAYERS
+    sweep = DecodeSweep(args.m, rank, world, device,
+                        kinds=tuple(args.layer) if args.layer else None, n_layers=args.layers)
     if world > 1:
         warm = torch.ones(1, device=device)
         dist.all_reduce(warm)
@@ -397,8 +482,15 @@ def main() -> None:
     graph = capture(sweep.step, device)
     for _ in range(args.warmup):
         graph.replay()
+    # Settle phase: about one second of untimed replays so the clocks seen by the sampler are
+    # the ones under sustained load. The count is agreed over ranks (the graph holds NCCL calls).
+    one = torch.tensor([time_graph(graph, 1, device, barrier)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(one, op=dist.ReduceOp.MAX)
+    settle = int(min(2000, max(3, 1000.0 / max(float(one.item()), 1e-3))))
     with ClockSampler(local) as clocks:
-        ms_total = time_graph(graph, args.steps, device, barrier)
+        time_graph(graph, settle, device, barrier)
+        ms_total = time_graph(graph, args.steps, device, barrier, clocks)
     ms = ms_total / args.steps
     t = torch.tensor([ms], device=device, dtype=torch.float64)
     b = torch.tensor([sweep.bytes_per_step], device=device, dtype=torch.float64)
@@ -413,31 +505,32 @@ def main() -> None:
     # back to back as a graph, timed with CUDA events; algorithmic bytes / mean launch time.
     per_kind = {}
     kind_bytes = kind_ms = 0.0
-    for name, *_ in LAYER_SHAPES:
+    for name in sweep.kinds:
         g = capture(lambda name=name: sweep.step(only=name, allreduce=False), device)
         for _ in range(3):
             g.replay()
         reps = max(3, args.steps // 2)
-        kms = time_graph(g, reps, device) / reps / LAYERS
+        kms = time_graph(g, reps, device) / reps / sweep.n_layers
         nn, kk = sweep.shard_shapes[name]
         kb = algorithmic_bytes(args.m, nn, kk)
         per_kind[name] = {"n": nn, "k": kk, "us_per_launch": round(kms * 1e3, 3),
                           "gbs": round(kb / (kms * 1e-3) / 1e9, 1)}
-        kind_bytes += kb * LAYERS
-        kind_ms += kms * LAYERS
+        kind_bytes += kb * sweep.n_layers
+        kind_ms += kms * sweep.n_layers
         del g
     achieved = kind_bytes / (kind_ms * 1e-3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "gemv_dram_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("bytes_per_step_tp1")
+    traffic = dram_traffic(sweep.kinds, sweep.n_layers, args.m, world)
+    if traffic:
+        for name in sweep.kinds:
+            per_kind[name]["dram_bytes"] = traffic["per_launch"][name]
 
     # End to end through the C ABI with host buffers: pinned H2D of the step's activations,
     # 112 eager tf_w4a16_linear calls (plus the all-reduces), D2H of the step's last output.
     h_in = [torch.empty_like(x, device="cpu").pin_memory() for x in (sweep.x_h, sweep.x_o, sweep.x_d)]
     for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
         hbuf.copy_(x.cpu())
-    h_out = torch.empty_like(sweep.y["down"], device="cpu").pin_memory()
+    y_last = sweep.y[sweep.kinds[-1]]
+    h_out = torch.empty_like(y_last, device="cpu").pin_memory()
     h2d = sum(h.numel() * h.element_size() for h in h_in)
     d2h = h_out.numel() * h_out.element_size()
 
@@ -445,7 +538,7 @@ def main() -> None:
         for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
             x.copy_(hbuf, non_blocking=True)
         sweep.step()
-        h_out.copy_(sweep.y["down"], non_blocking=True)
+        h_out.copy_(y_last, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -470,13 +563,12 @@ def main() -> None:
     if world == 1 and not args.skip_gemm:
         gemm = gemm_metric(device, args.gemm_m, max(3, args.steps // 2), 3, pk, src)
     cpu = None
-    if rank == 0 and world == 1 and not args.skip_cpu:
-        cpu = cpu_baseline(args.m, reps=1)
+    if rank == 0 and world == 1 and full and not args.skip_cpu:
+        cpu = cpu_baseline(args.m, min_seconds=10.0)
 
     if rank == 0:
         line = {
-            "metric": "W4A16 GEMV HBM GB/s at M=1 (Qwen2.5-7B decode sweep, 28 layers)"
-                      if args.m == 1 else f"W4A16 GEMV HBM GB/s at M={args.m} (Qwen2.5-7B decode sweep)",
+            "metric": metric_name(args.m),
             "value": round(value, 2),
             "unit": "GB/s",
             "n_gpus": world,
@@ -489,19 +581,23 @@ def main() -> None:
             "dtype": "int4xfp16->fp32",
             "data": "synthetic",
             "config": {
-                "workload": f"config3 decode sweep: 28 layers x (qkv, o, gate_up, down), M={args.m}, "
-                            f"TP={world}, CUDA-graph replay",
+                "workload": f"config3 decode sweep: {sweep.n_layers} layers x ({', '.join(sweep.kinds)}), "
+                            f"M={args.m}, TP={world}, CUDA-graph replay",
                 "m": args.m, "group_size": G, "tp": world,
                 "parallelism": f"tp{world}" + (" (NCCL all-reduce after o/down)" if world > 1 else ""),
-                "l2": "inputs larger than L2 (3.4 GB of weights streamed per step)",
+                "l2": f"inputs larger than L2 ({total_bytes / 1e9:.2f} GB of weights streamed per step)",
                 "pdl": not args.no_pdl,
                 "bytes_per_step": int(total_bytes),
             },
             "roofline": {
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": traffic["bytes_per_step"] if traffic else None,
+                "algorithmic_bytes": int(kind_bytes),
+                "per": "step (all GEMV launches of one sweep; achieved = algorithmic bytes / summed "
+                       "per-launch device time)",
                 "peak_source": f"{src} hbm_gbs",
-                "kernel": "w4a16_mma_kernel (GEMV, M<=8)",
+                "kernel": "w4a16_gemv_kernel (decode GEMV, M<=8)",
                 "per_layer": per_kind,
             },
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,

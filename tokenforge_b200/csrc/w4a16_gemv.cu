@@ -14,10 +14,9 @@
 //   * the warp walks a contiguous range of 128-wide K blocks; lane c reads 16 bytes (k in
 //     [128b + 32c, +32)) of each of its rows, so a quad reads 64 contiguous bytes per row;
 //   * the CTA's activations x[0:M, k-range] are staged once in shared memory;
-//   * weights, scales and zero points are loaded into registers two blocks ahead, and requested
-//     from L2 kPrefetch blocks ahead, four blocks (256 bytes per row) per bulk prefetch, so the
-//     register loads only wait for L2; the first loads are issued before the
-//     programmatic-dependent-launch wait;
+//   * weights, scales and zero points are loaded into registers two blocks ahead through four
+//     row pointers kept in registers (no L2 prefetch: measured, its address work cost more than
+//     it hid); the first loads are issued before the programmatic-dependent-launch wait;
 //   * rows beyond N and tokens beyond M are clamped for loading (never stored); only a partial
 //     last K block takes predicated loads;
 //   * unpack and dequant are PTX (lop3, sub.rn / mul.rn.f16x2): exactly three instructions per
@@ -38,7 +37,6 @@ namespace {
 constexpr int kKB = 128;         // K values per block
 constexpr int kCtaWarps = 8;     // warps per CTA (WARPS_N x WARPS_K)
 constexpr int kWarpRows = 32;    // weight rows per warp tile
-constexpr int kPrefetch = 8;     // L2 prefetch distance in blocks (issued four blocks at a time)
 
 struct GemvParams {
   const __half* x;
@@ -65,11 +63,10 @@ struct GSlot {
 };
 
 struct GLane {
-  const int32_t* w;     // row r0 (first of the lane's four) + this lane's word offset 4c
+  const int32_t* w[4];  // rows r0..r0+3 (the lane's four) + this lane's word offset 4c
   const uint2* s;       // scales row 0, column r0 (4 halves)
   const int32_t* z;     // qzeros row 0, word r0 / 8
   const uint4* xs;      // staged activations: token row q (clamped), + 32c
-  int64_t ldw;          // words per packed row
   int nib[4];           // bit offsets of the four rows' zero points in the qzeros word
   int kb0, b_end;       // this CTA's first block, this warp's end block (exclusive)
   int c;
@@ -77,50 +74,31 @@ struct GLane {
 
 __device__ __forceinline__ uint4 zero4() { return make_uint4(0, 0, 0, 0); }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// L2 prefetch of blocks [bb, bb + nb) of this warp's rows: lane c == 0 of each quad asks for the
-// nb * 64 contiguous bytes of each of its four rows (one bulk prefetch per row), lane 0 for the
-// scales and qzeros lines of those blocks' groups.
-__device__ __forceinline__ void gprefetch(int bb, int nb, const GemvParams& p, const GLane& L) {
-  if (nb <= 0) return;
-  if (L.c == 0) {
-    const int32_t* r = L.w + bb * (kKB / 8);  // c == 0: the row's segment starts here
-#pragma unroll
-    for (int j = 0; j < 4; ++j) bulk_prefetch_l2(r + j * L.ldw, static_cast<uint32_t>(nb) * 64u);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    for (int t = 0; t < nb; ++t) {
-      const int g = ((bb + t) * kKB) >> p.group_shift;
-      prefetch_l2(L.s + g * (p.N >> 2));
-      prefetch_l2(L.z + g * (p.N >> 3));
-    }
-  }
-}
-
 __device__ __forceinline__ void gload(GSlot& s, int bb, const GemvParams& p, const GLane& L) {
   if (bb >= L.b_end) return;  // warp-uniform: the slot is never consumed
   const int k = bb * kKB + 32 * L.c;
   const int g = k >> p.group_shift;
-  const int32_t* r = L.w + bb * (kKB / 8);
   if ((bb + 1) * kKB <= p.K) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s.w[j] = ldg_stream_v4(r + j * L.ldw);
+    for (int j = 0; j < 4; ++j) s.w[j] = ldg_stream_v4(L.w[j] + bb * (kKB / 8));
     s.s = __ldg(L.s + g * (p.N >> 2));
     s.z = static_cast<uint32_t>(__ldg(L.z + g * (p.N >> 3)));
   } else {  // partial last block: a chunk past K reads as zero weights, scale 0, zero point 0
     const bool in = k < p.K;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s.w[j] = in ? ldg_stream_v4(r + j * L.ldw) : zero4();
+    for (int j = 0; j < 4; ++j) s.w[j] = in ? ldg_stream_v4(L.w[j] + bb * (kKB / 8)) : zero4();
     s.s = in ? __ldg(L.s + g * (p.N >> 2)) : make_uint2(0u, 0u);
     s.z = in ? static_cast<uint32_t>(__ldg(L.z + g * (p.N >> 3))) : 0u;
   }
+}
+
+// Group size 128: block bb is group bb and K % 128 == 0, so every block is whole.
+__device__ __forceinline__ void gload_grp(GSlot& s, int bb, const GemvParams& p, const GLane& L) {
+  if (bb >= L.b_end) return;  // warp-uniform: the slot is never consumed
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s.w[j] = ldg_stream_v4(L.w[j] + bb * (kKB / 8));
+  s.s = __ldg(L.s + bb * (p.N >> 2));
+  s.z = static_cast<uint32_t>(__ldg(L.z + bb * (p.N >> 3)));
 }
 
 // PTX forms: one LOP3 per pair, and the fp16 subtract / multiply with explicit .rn so they are
@@ -185,6 +163,92 @@ __device__ __forceinline__ void gcompute(float (&acc)[2][2][4], const GSlot& s, 
   }
 }
 
+// mma.m16n8k16 with a zero accumulator input: d = a * b.
+__device__ __forceinline__ void mma_16816_zc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                             uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// Group-size-128 block (one K block is one quantization group): the scale moves out of the
+// per-weight work. Each pair is unpacked to the exact fp16 integer pair (q - z): bits 0-3 of a
+// half ORed into 0x6400 read as 1024 + q and bits 4-7 ORed into 0x5400 read as 64 + q, so one
+// LOP3 and one HSUB2 of (1024 + z) or (64 + z) give q - z for either nibble position (one shift
+// per word brings the upper byte of each half down). The tensor core sums x * (q - z) exactly
+// into fp32 and the block's sum is multiplied by the row's scale once: no fp16 weight is rounded,
+// q == z contributes exactly zero, and Inf / NaN activations propagate as through the dequant.
+__device__ __forceinline__ void gcompute_grp(float (&acc)[2][2][4], const GSlot& s, int bb,
+                                             const GLane& L) {
+  const uint32_t m0 = 0x000F000Fu, m1 = 0x00F000F0u;
+  const uint32_t g0 = 0x64006400u, g1 = 0x54005400u;
+  uint32_t z0[4], z1[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t z = (s.z >> L.nib[j]) & 0xFu;
+    z0[j] = (z * 0x00010001u) | g0;  // (1024 + z, 1024 + z)
+    z1[j] = (z * 0x00100010u) | g1;  // (64 + z, 64 + z)
+  }
+  const uint4* xp = L.xs + (bb - L.kb0) * (kKB / 8);
+  const uint32_t w[4][4] = {{s.w[0].x, s.w[0].y, s.w[0].z, s.w[0].w},
+                            {s.w[1].x, s.w[1].y, s.w[1].z, s.w[1].w},
+                            {s.w[2].x, s.w[2].y, s.w[2].z, s.w[2].w},
+                            {s.w[3].x, s.w[3].y, s.w[3].z, s.w[3].w}};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 xv = xp[i];
+    uint32_t pa[4], pb[4], pc[4], pd[4];  // offsets (0,1), (2,3), (4,5), (6,7) of row j's word i
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t h = w[j][i] >> 8;
+      pa[j] = hsub2_rn(lop_mask_or(w[j][i], m0, g0), z0[j]);
+      pb[j] = hsub2_rn(lop_mask_or(w[j][i], m1, g1), z1[j]);
+      pc[j] = hsub2_rn(lop_mask_or(h, m0, g0), z0[j]);
+      pd[j] = hsub2_rn(lop_mask_or(h, m1, g1), z1[j]);
+    }
+    // Tile 0: fragment rows q / q+8 <- rows 4q / 4q+1; tile 1 <- rows 4q+2 / 4q+3.
+    const uint32_t t0a[4] = {pa[0], pa[1], pb[0], pb[1]}, t0b[4] = {pc[0], pc[1], pd[0], pd[1]};
+    const uint32_t t1a[4] = {pa[2], pa[3], pb[2], pb[3]}, t1b[4] = {pc[2], pc[3], pd[2], pd[3]};
+    if (i == 0) {
+      mma_16816_zc(acc[0][0], t0a, xv.x, xv.y);
+      mma_16816_zc(acc[0][1], t0b, xv.z, xv.w);
+      mma_16816_zc(acc[1][0], t1a, xv.x, xv.y);
+      mma_16816_zc(acc[1][1], t1b, xv.z, xv.w);
+    } else {
+      mma_16816(acc[0][0], t0a, xv.x, xv.y);
+      mma_16816(acc[0][1], t0b, xv.z, xv.w);
+      mma_16816(acc[1][0], t1a, xv.x, xv.y);
+      mma_16816(acc[1][1], t1b, xv.z, xv.w);
+    }
+  }
+}
+
+// y += s * (block sum) for the lane's four rows (row 4q + j: tile j / 2, fragment values
+// 2 (j % 2) and 2 (j % 2) + 1, tokens 2c and 2c + 1).
+__device__ __forceinline__ void fold_grp(float (&y)[2][4], const float (&acc)[2][2][4],
+                                         const GSlot& s) {
+  const uint32_t sp[2] = {s.s.x, s.s.y};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sh = (j & 1) ? (sp[j >> 1] >> 16) : (sp[j >> 1] & 0xFFFFu);
+    const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sh)));
+    const int t = j >> 1, e = 2 * (j & 1);
+    y[t][e] = fmaf(sf, acc[t][0][e] + acc[t][1][e], y[t][e]);
+    y[t][e + 1] = fmaf(sf, acc[t][0][e + 1] + acc[t][1][e + 1], y[t][e + 1]);
+  }
+}
+
+// True if any of the lane's four scales of this block is Inf or NaN (exponent all ones): such a
+// block takes the per-weight dequant so that fp16(q - z) * s keeps its Inf / NaN pattern.
+// Adding 0x0400 to a half's exponent bits carries into bit 15 only when they are all ones.
+__device__ __forceinline__ bool scales_nonfinite(const GSlot& s) {
+  const uint32_t t =
+      ((s.s.x & 0x7C007C00u) + 0x04000400u) | ((s.s.y & 0x7C007C00u) + 0x04000400u);
+  return (t & 0x80008000u) != 0;
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -203,7 +267,7 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
-template <int WARPS_N, int WARPS_K, bool kCluster>
+template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact>
 __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const GemvParams p) {
   static_assert(WARPS_N * WARPS_K == kCtaWarps, "CTA shape");
   extern __shared__ uint4 xs_smem[];
@@ -225,8 +289,9 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   const int share = (kb1 - L.kb0 + WARPS_K - 1) / WARPS_K;
   const int b0 = L.kb0 + wk * share;
   L.b_end = min(kb1, b0 + share);
-  L.ldw = p.K / 8;
-  L.w = p.qw + r0 * L.ldw + 4 * L.c;
+  const int ldw = p.K / 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) L.w[j] = p.qw + (r0 + j) * ldw + 4 * L.c;
   L.s = reinterpret_cast<const uint2*>(p.scales + r0);
   L.z = p.qzeros + (r0 >> 3);
 #pragma unroll
@@ -235,13 +300,15 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   L.xs = xs_smem + (xq * p.xs_stride + 32 * L.c) / 8;
   const uint32_t mask = 0x000F000Fu, magic = 0x64006400u;
 
-  // Weights, scales and zero points never depend on the preceding kernel: the L2 prefetches of
-  // the first blocks and the register loads of the first two are issued before the
-  // programmatic-dependent-launch wait.
-  gprefetch(b0 + 2, min(b0 + 2 + kPrefetch, L.b_end) - (b0 + 2), p, L);
+  // Weights, scales and zero points never depend on the preceding kernel: the register loads of
+  // the first two blocks are issued before the programmatic-dependent-launch wait.
   GSlot s0, s1;
-  gload(s0, b0, p, L);
-  gload(s1, b0 + 1, p, L);
+  auto load = [&](GSlot& sl, int b) {
+    if constexpr (kFact) gload_grp(sl, b, p, L);
+    else gload(sl, b, p, L);
+  };
+  load(s0, b0);
+  load(s1, b0 + 1);
   pdl_wait();
 
   // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory.
@@ -259,18 +326,45 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   __syncthreads();
 
   float acc[2][2][4] = {};
-  for (int b = b0; b < L.b_end; b += 2) {
-    if (((b - b0) & 3) == 2) {  // every fourth block: the four blocks kPrefetch ahead
-      const int pb = b + kPrefetch;
-      gprefetch(pb, min(4, L.b_end - pb), p, L);
+  float y[2][4] = {};
+  auto step = [&](const GSlot& sl, int b) {
+    if constexpr (kFact) {
+      if (!__any_sync(0xffffffffu, scales_nonfinite(sl))) {
+        gcompute_grp(acc, sl, b, L);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[t][0][r] = acc[t][1][r] = 0.f;
+        gcompute(acc, sl, b, L, mask, magic);
+        // gcompute's sums already carry the scale: fold them with a unit scale.
+        GSlot one = sl;
+        one.s = make_uint2(0x3C003C00u, 0x3C003C00u);
+        fold_grp(y, acc, one);
+        return;
+      }
+      fold_grp(y, acc, sl);
+    } else {
+      gcompute(acc, sl, b, L, mask, magic);
     }
-    gcompute(acc, s0, b, L, mask, magic);
-    gload(s0, b + 2, p, L);
+  };
+  for (int b = b0; b < L.b_end; b += 2) {
+    step(s0, b);
+    load(s0, b + 2);
     if (b + 1 >= L.b_end) break;
-    gcompute(acc, s1, b + 1, L, mask, magic);
-    gload(s1, b + 3, p, L);
+    step(s1, b + 1);
+    load(s1, b + 3);
   }
   pdl_launch_dependents();
+  if constexpr (kFact) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        acc[t][0][r] = y[t][r];
+        acc[t][1][r] = 0.f;
+      }
+  }
 
   // Fixed-order reductions: the accumulator chains, then the WARPS_K warps (warp order), then the
   // CTAs of the cluster (rank order).
@@ -352,10 +446,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   y[m * ldy + n] = __float2half_rn(s);
 }
 
-template <int WN, int WK, bool kCluster>
+template <int WN, int WK, bool kCluster, bool kFact>
 int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
                         cudaStream_t stream, bool pdl) {
-  auto kern = w4a16_gemv_kernel<WN, WK, kCluster>;
+  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact>;
   if (smem > 48 * 1024) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -393,14 +487,14 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
   return TF_OK;
 }
 
-template <bool kCluster>
+template <bool kCluster, bool kFact>
 int launch_gemv_shape(const LinearPlan& plan, const GemvParams& p, size_t smem, cudaStream_t st,
                       bool pdl) {
   switch (plan.warps_k) {
-    case 1: return launch_gemv_variant<8, 1, kCluster>(plan, p, smem, st, pdl);
-    case 2: return launch_gemv_variant<4, 2, kCluster>(plan, p, smem, st, pdl);
-    case 4: return launch_gemv_variant<2, 4, kCluster>(plan, p, smem, st, pdl);
-    case 8: return launch_gemv_variant<1, 8, kCluster>(plan, p, smem, st, pdl);
+    case 1: return launch_gemv_variant<8, 1, kCluster, kFact>(plan, p, smem, st, pdl);
+    case 2: return launch_gemv_variant<4, 2, kCluster, kFact>(plan, p, smem, st, pdl);
+    case 4: return launch_gemv_variant<2, 4, kCluster, kFact>(plan, p, smem, st, pdl);
+    case 8: return launch_gemv_variant<1, 8, kCluster, kFact>(plan, p, smem, st, pdl);
     default: return TF_ERR_INVALID_ARG;
   }
 }
@@ -433,8 +527,16 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   p.partial = outer > 1 ? static_cast<float*>(a.workspace) : nullptr;
   const size_t smem = gemv_smem_bytes(a.M, plan.blocks_per_split);
   const bool pdl = (launch_flags() & TF_LAUNCH_PDL) != 0;
-  const int st = plan.cluster > 1 ? launch_gemv_shape<true>(plan, p, smem, stream, pdl)
-                                  : launch_gemv_shape<false>(plan, p, smem, stream, pdl);
+  // Group size 128 (one K block per group): the scale is applied once per block after the
+  // tensor-core sums; other group sizes dequantize every weight.
+  const bool fact = a.group_size == kKB;
+  int st;
+  if (plan.cluster > 1)
+    st = fact ? launch_gemv_shape<true, true>(plan, p, smem, stream, pdl)
+              : launch_gemv_shape<true, false>(plan, p, smem, stream, pdl);
+  else
+    st = fact ? launch_gemv_shape<false, true>(plan, p, smem, stream, pdl)
+              : launch_gemv_shape<false, false>(plan, p, smem, stream, pdl);
   if (st != TF_OK || outer == 1) return st;
   return launch_splitk_reduce(p.partial, outer, a.M, a.N, a.bias, a.y, a.ldy, stream);
 }
