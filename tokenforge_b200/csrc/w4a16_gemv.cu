@@ -184,12 +184,19 @@ __device__ __forceinline__ void gcompute_grp(float (&acc)[2][2][4], const GSlot&
                                              const GLane& L) {
   const uint32_t m0 = 0x000F000Fu, m1 = 0x00F000F0u;
   const uint32_t g0 = 0x64006400u, g1 = 0x54005400u;
+  // The four rows' zero points sit in nibbles {0, 4, 1, 5} of the qzeros word shifted by nib[0]
+  // (0 or 8): one LOP3 per row pair gives (1024 + z_a, 1024 + z_b), a byte permute broadcasts each
+  // row's value to both halves, and 1024 + z - 960 = 64 + z exactly.
   uint32_t z0[4], z1[4];
+  {
+    const uint32_t zs = s.z >> L.nib[0];
+    const uint32_t a = lop_mask_or(zs, m0, g0), b = lop_mask_or(zs >> 4, m0, g0);
+    z0[0] = __byte_perm(a, a, 0x1010u);
+    z0[1] = __byte_perm(a, a, 0x3232u);
+    z0[2] = __byte_perm(b, b, 0x1010u);
+    z0[3] = __byte_perm(b, b, 0x3232u);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t z = (s.z >> L.nib[j]) & 0xFu;
-    z0[j] = (z * 0x00010001u) | g0;  // (1024 + z, 1024 + z)
-    z1[j] = (z * 0x00100010u) | g1;  // (64 + z, 64 + z)
+    for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
   }
   const uint4* xp = L.xs + (bb - L.kb0) * (kKB / 8);
   const uint32_t w[4][4] = {{s.w[0].x, s.w[0].y, s.w[0].z, s.w[0].w},
@@ -213,19 +220,17 @@ __device__ __forceinline__ void gcompute_grp(float (&acc)[2][2][4], const GSlot&
     const uint32_t t1a[4] = {pa[2], pa[3], pb[2], pb[3]}, t1b[4] = {pc[2], pc[3], pd[2], pd[3]};
     if (i == 0) {
       mma_16816_zc(acc[0][0], t0a, xv.x, xv.y);
-      mma_16816_zc(acc[0][1], t0b, xv.z, xv.w);
       mma_16816_zc(acc[1][0], t1a, xv.x, xv.y);
-      mma_16816_zc(acc[1][1], t1b, xv.z, xv.w);
     } else {
       mma_16816(acc[0][0], t0a, xv.x, xv.y);
-      mma_16816(acc[0][1], t0b, xv.z, xv.w);
       mma_16816(acc[1][0], t1a, xv.x, xv.y);
-      mma_16816(acc[1][1], t1b, xv.z, xv.w);
     }
+    mma_16816(acc[0][0], t0b, xv.z, xv.w);
+    mma_16816(acc[1][0], t1b, xv.z, xv.w);
   }
 }
 
-// y += s * (block sum) for the lane's four rows (row 4q + j: tile j / 2, fragment values
+// y += s * (block sum, one accumulator chain per tile) for the lane's four rows (row 4q + j: tile j / 2, fragment values
 // 2 (j % 2) and 2 (j % 2) + 1, tokens 2c and 2c + 1).
 __device__ __forceinline__ void fold_grp(float (&y)[2][4], const float (&acc)[2][2][4],
                                          const GSlot& s) {
@@ -235,18 +240,9 @@ __device__ __forceinline__ void fold_grp(float (&y)[2][4], const float (&acc)[2]
     const uint32_t sh = (j & 1) ? (sp[j >> 1] >> 16) : (sp[j >> 1] & 0xFFFFu);
     const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sh)));
     const int t = j >> 1, e = 2 * (j & 1);
-    y[t][e] = fmaf(sf, acc[t][0][e] + acc[t][1][e], y[t][e]);
-    y[t][e + 1] = fmaf(sf, acc[t][0][e + 1] + acc[t][1][e + 1], y[t][e + 1]);
+    y[t][e] = fmaf(sf, acc[t][0][e], y[t][e]);
+    y[t][e + 1] = fmaf(sf, acc[t][0][e + 1], y[t][e + 1]);
   }
-}
-
-// True if any of the lane's four scales of this block is Inf or NaN (exponent all ones): such a
-// block takes the per-weight dequant so that fp16(q - z) * s keeps its Inf / NaN pattern.
-// Adding 0x0400 to a half's exponent bits carries into bit 15 only when they are all ones.
-__device__ __forceinline__ bool scales_nonfinite(const GSlot& s) {
-  const uint32_t t =
-      ((s.s.x & 0x7C007C00u) + 0x04000400u) | ((s.s.y & 0x7C007C00u) + 0x04000400u);
-  return (t & 0x80008000u) != 0;
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -329,20 +325,7 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   float y[2][4] = {};
   auto step = [&](const GSlot& sl, int b) {
     if constexpr (kFact) {
-      if (!__any_sync(0xffffffffu, scales_nonfinite(sl))) {
-        gcompute_grp(acc, sl, b, L);
-      } else {
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) acc[t][0][r] = acc[t][1][r] = 0.f;
-        gcompute(acc, sl, b, L, mask, magic);
-        // gcompute's sums already carry the scale: fold them with a unit scale.
-        GSlot one = sl;
-        one.s = make_uint2(0x3C003C00u, 0x3C003C00u);
-        fold_grp(y, acc, one);
-        return;
-      }
+      gcompute_grp(acc, sl, b, L);
       fold_grp(y, acc, sl);
     } else {
       gcompute(acc, sl, b, L, mask, magic);
@@ -357,6 +340,29 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   }
   pdl_launch_dependents();
   if constexpr (kFact) {
+    // A non-finite activation or scale makes some y non-finite (fp32 sums of finite fp16
+    // products cannot overflow). Then the warp recomputes its range with the per-weight dequant
+    // fp16(q - z) * s, whose Inf / NaN pattern is the reference's (an Inf scale times q == z is
+    // NaN there, while the block-scaled sum would give Inf).
+    bool bad = false;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) bad |= !isfinite(y[t][r]);
+    if (__any_sync(0xffffffffu, bad)) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[t][0][r] = acc[t][1][r] = 0.f;
+      for (int b = b0; b < L.b_end; ++b) {
+        gload_grp(s0, b, p, L);
+        gcompute(acc, s0, b, L, mask, magic);
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) y[t][r] = acc[t][0][r] + acc[t][1][r];
+    }
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
