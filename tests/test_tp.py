@@ -1,0 +1,137 @@
+"""Tensor-parallel sharding (Qwen2.5-7B decode layers): shard bounds, shard contents against
+the unsharded layer, and the row-parallel all-reduce / column-parallel gather over two gloo
+ranks on CPU, with the oracle's fp64 product standing in for the kernel (the host logic is
+what is under test; the kernels have their own GPU parity suite)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle
+from tests.numerics import cases
+from tests.numerics.tolerance import atol
+from tokenforge_b200 import tp
+from tokenforge_b200.pack import W4A16Weights
+
+G = 128
+
+
+def test_split_even_sizes_and_order() -> None:
+    assert tp.split_even(10, 3) == [(0, 4), (4, 7), (7, 10)]
+    assert tp.split_even(4, 4) == [(0, 1), (1, 2), (2, 3), (3, 4)]
+    assert tp.split_even(2, 4) == [(0, 1), (1, 2), (2, 2), (2, 2)]
+    with pytest.raises(ValueError):
+        tp.split_even(5, 0)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("n", [4608, 37888, 3584])
+def test_column_bounds_cover_n_in_whole_words(n: int, world: int) -> None:
+    b = tp.column_bounds(n, world)
+    assert b[0][0] == 0 and b[-1][1] == n
+    assert all(hi == lo for (_, hi), (lo, _) in zip(b, b[1:]))
+    assert all(lo % 8 == 0 and hi % 8 == 0 for lo, hi in b)
+    sizes = [hi - lo for lo, hi in b]
+    assert max(sizes) - min(sizes) <= 8
+
+
+def test_row_bounds_are_group_aligned_and_uneven_at_tp8() -> None:
+    # Qwen2.5-7B o (K = 3584, 28 groups) and down (K = 18944, 148 groups) at TP = 8.
+    o = tp.row_bounds(3584, G, 8)
+    assert [(hi - lo) // G for lo, hi in o] == [4, 4, 4, 4, 3, 3, 3, 3]
+    down = tp.row_bounds(18944, G, 8)
+    assert [(hi - lo) // G for lo, hi in down] == [19, 19, 19, 19, 18, 18, 18, 18]
+    assert tp.row_bounds(3584, G, 2) == [(0, 1792), (1792, 3584)]
+    with pytest.raises(ValueError):
+        tp.row_bounds(3584 + 64, G, 2)
+
+
+def test_shards_hold_exactly_the_layer_slices() -> None:
+    w = cases.layer_weights(64, 512, 7)
+    full = oracle.dequantize_tf(w.qweight_t, w.scales, w.qzeros, G)
+    for world in (2, 4):
+        for r in range(world):
+            col = tp.shard_layer(w, "column", r, world)
+            n0, n1 = col.bounds
+            got = oracle.dequantize_tf(col.weights.qweight_t, col.weights.scales,
+                                       col.weights.qzeros, G)
+            assert torch.equal(got.view(torch.int16), full[n0:n1].view(torch.int16))
+            row = tp.shard_layer(w, "row", r, world)
+            k0, k1 = row.bounds
+            got = oracle.dequantize_tf(row.weights.qweight_t, row.weights.scales,
+                                       row.weights.qzeros, G)
+            assert torch.equal(got.view(torch.int16), full[:, k0:k1].view(torch.int16))
+
+
+def test_bias_goes_to_column_slices_and_rank0_rows() -> None:
+    w = cases.layer_weights(64, 256, 1)
+    b = cases.bias(64, 1)
+    assert torch.equal(tp.shard_layer(w, "column", 1, 2, b).bias, b[32:])
+    assert tp.shard_layer(w, "row", 0, 2, b).bias is b
+    assert tp.shard_layer(w, "row", 1, 2, b).bias is None
+    with pytest.raises(ValueError):
+        tp.shard_layer(w, "diagonal", 0, 2)
+
+
+def _oracle_linear(x: torch.Tensor, w: W4A16Weights, b: torch.Tensor | None) -> torch.Tensor:
+    return oracle.w4a16_reference(x, w.qweight_t, w.scales, w.qzeros, w.group_size, b).to(
+        torch.float16)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return int(s.getsockname()[1])
+
+
+def _rank_main(rank: int, world: int, port: int, out: dict) -> None:  # type: ignore[type-arg]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, n, k = 3, 64, 1024
+        w = cases.layer_weights(n, k, 11)
+        b = cases.bias(n, 11)
+        x = cases.activations(m, k, 11)
+        row = tp.shard_layer(w, "row", rank, world, b)
+        y_row = tp.linear_shard(x, row, linear=_oracle_linear)
+        col = tp.shard_layer(w, "column", rank, world, b)
+        y_col = tp.linear_shard(x, col, linear=_oracle_linear)
+        parts = [torch.empty_like(y_col) for _ in range(world)]
+        dist.all_gather(parts, y_col)
+        if rank == 0:
+            out["row"] = y_row
+            out["col"] = torch.cat(parts, dim=1)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_two_gloo_ranks_reassemble_the_full_layer(world: int) -> None:
+    m, n, k = 3, 64, 1024
+    w = cases.layer_weights(n, k, 11)
+    b = cases.bias(n, 11)
+    x = cases.activations(m, k, 11)
+    with mp.get_context("spawn").Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world,
+                           start_method="spawn")
+        y_row, y_col = out["row"], out["col"]
+    # Row-parallel: the all-reduce sums the ranks' fp16 partials; with two ranks the sum is
+    # the same single rounding whatever the order.
+    partials = [_oracle_linear(x[:, k0:k1], tp.shard_rows(w, k0, k1), b if r == 0 else None)
+                for r, (k0, k1) in enumerate(tp.row_bounds(k, G, world))]
+    assert torch.equal(y_row, partials[0] + partials[1])
+    # Column-parallel: the gathered columns are the unsharded product, bit for bit.
+    full = _oracle_linear(x, w, b)
+    assert torch.equal(y_col, full)
+    # And the row-parallel result is the full product within the W4A16 tolerance.
+    ref = oracle.w4a16_reference(x, w.qweight_t, w.scales, w.qzeros, G, b)
+    w16 = oracle.dequantize_tf(w.qweight_t, w.scales, w.qzeros, G)
+    assert float((y_row.double() - ref).abs().max()) <= 2 * atol(x, w16, "cpu") + 2e-3

@@ -100,18 +100,25 @@ def shard_layer(
     raise ValueError(f"kind must be 'column' or 'row', got {kind!r}")
 
 
-def linear_shard(x: torch.Tensor, shard: LayerShard, group=None) -> torch.Tensor:  # type: ignore[no-untyped-def]
+def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None) -> torch.Tensor:  # type: ignore[no-untyped-def]
     """Run one rank's shard. Column-parallel returns this rank's columns; row-parallel takes
-    the full activations, uses its K slice, and all-reduces the fp16 partials in place."""
+    the full activations, uses its K slice, and all-reduces the fp16 partials in place.
+
+    ``linear(x, weights, bias) -> fp16 [M, N]`` computes the local product; by default the
+    kernel library's launch table (GEMV for M <= 8, tensor-core GEMM above)."""
     import torch.distributed as dist
 
-    from tokenforge_b200.ops import w4a16_gemm
+    if linear is None:
+        from tokenforge_b200.ops import w4a16_gemm
+
+        def linear(xx, w, b):  # type: ignore[no-untyped-def]
+            return w4a16_gemm(xx, w.qweight_t, w.scales, w.qzeros, w.group_size, b)
 
     w = shard.weights
     if shard.kind == "column":
-        return w4a16_gemm(x, w.qweight_t, w.scales, w.qzeros, w.group_size, shard.bias)
+        return linear(x, w, shard.bias)
     k0, k1 = shard.bounds
-    y = w4a16_gemm(x[:, k0:k1], w.qweight_t, w.scales, w.qzeros, w.group_size, shard.bias)
+    y = linear(x[:, k0:k1], w, shard.bias)
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
