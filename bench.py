@@ -171,12 +171,18 @@ class DecodeSweep:
     """This rank's shards of the 28-layer sweep plus the C-ABI argument tuples of a step."""
 
     def __init__(self, m: int, rank: int, world: int, device: torch.device, seed: int = 0,
-                 kinds: tuple[str, ...] | None = None, n_layers: int = LAYERS) -> None:
+                 kinds: tuple[str, ...] | None = None, n_layers: int = LAYERS,
+                 peers=None) -> None:  # type: ignore[no-untyped-def]
         from tokenforge_b200 import _lib, tp
         from tokenforge_b200.pack import W4A16Weights
 
         self.m, self.rank, self.world, self.device = m, rank, world, device
         self.n_layers = n_layers
+        # Row-parallel layers whose all-reduce runs fused in the GEMV (same decision on every
+        # rank: it depends on the global shape only).
+        self.peers = peers
+        self.fused = {name: bool(peers is not None and peers.supports(m, n, k, G))
+                      for name, n, k, kind in LAYER_SHAPES if kind == "row"}
         shapes = [s for s in LAYER_SHAPES if kinds is None or s[0] in kinds]
         self.kinds = [s[0] for s in shapes]
         self.lib = _lib.lib()
@@ -244,6 +250,12 @@ class DecodeSweep:
         fn = self.lib.tf_w4a16_linear
         for name, args in self.calls:
             if only is not None and name != only:
+                continue
+            if self.world > 1 and self.fused.get(name, False):
+                st = self.lib.tf_w4a16_linear_allreduce(*args, ctypes.byref(self.peers.peers),
+                                                         stream)
+                if st != 0:
+                    raise RuntimeError(f"tf_w4a16_linear_allreduce({name}) failed with status {st}")
                 continue
             st = fn(*args, stream)
             if st != 0:
@@ -440,6 +452,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--gemm-m", type=int, default=1024)
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--no-fuse", action="store_true",
+                    help="N > 1: all-reduce o/down with NCCL instead of inside the GEMV")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
     ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
@@ -472,8 +486,14 @@ def main() -> None:
     pk, src = peaks()
 
     full = args.layer is None and args.layers == LAYERS
+    peers = None
+    if world > 1 and not args.no_fuse:
+        from tokenforge_b200.tp import PeerMailbox
+
+        peers = PeerMailbox(max_m=8, max_n=HIDDEN, device=device)
     sweep = DecodeSweep(args.m, rank, world, device,
-                        kinds=tuple(args.layer) if args.layer else None, n_layers=args.layers)
+                        kinds=tuple(args.layer) if args.layer else None, n_layers=args.layers,
+                        peers=peers)
     if world > 1:
         warm = torch.ones(1, device=device)
         dist.all_reduce(warm)
@@ -509,8 +529,9 @@ def main() -> None:
         g = capture(lambda name=name: sweep.step(only=name, allreduce=False), device)
         for _ in range(3):
             g.replay()
+        torch.cuda.synchronize(device)
         reps = max(3, args.steps // 2)
-        kms = time_graph(g, reps, device) / reps / sweep.n_layers
+        kms = time_graph(g, reps, device, barrier) / reps / sweep.n_layers
         nn, kk = sweep.shard_shapes[name]
         kb = algorithmic_bytes(args.m, nn, kk)
         per_kind[name] = {"n": nn, "k": kk, "us_per_launch": round(kms * 1e3, 3),
@@ -584,7 +605,9 @@ def main() -> None:
                 "workload": f"config3 decode sweep: {sweep.n_layers} layers x ({', '.join(sweep.kinds)}), "
                             f"M={args.m}, TP={world}, CUDA-graph replay",
                 "m": args.m, "group_size": G, "tp": world,
-                "parallelism": f"tp{world}" + (" (NCCL all-reduce after o/down)" if world > 1 else ""),
+                "parallelism": f"tp{world}" + ("" if world == 1 else (
+                    " (o/down all-reduce fused into the GEMV over NVLink peer stores: "
+                    + ", ".join(k for k, v in sweep.fused.items() if v) + "; NCCL for the rest)")),
                 "l2": f"inputs larger than L2 ({total_bytes / 1e9:.2f} GB of weights streamed per step)",
                 "pdl": not args.no_pdl,
                 "bytes_per_step": int(total_bytes),
@@ -610,6 +633,10 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     del graph
+    if peers is not None:
+        if peers.error():
+            print("peer all-reduce: a wait timed out", file=sys.stderr)
+        peers.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -156,6 +156,54 @@ TF_API int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int6
                     const uint16_t* bias, int64_t N, int32_t group_size,
                     uint16_t* y, int64_t ldy, void* stream);
 
+/* ------------------------------------------------------- row-parallel all-reduce over NVLink
+ * Tensor-parallel o / down layers (row-split K) end in a sum of every rank's fp16 partial
+ * (NCCL all-reduce after o and down). tf_w4a16_linear_allreduce fuses that
+ * sum into the decode GEMV: each rank's GEMV epilogue writes its fp32 partial tile straight into
+ * every peer's mailbox (64-bit stores of value + call tag through CUDA IPC mappings over NVLink,
+ * no multicast), polls its own mailbox (bounded, 2 s) for the peers' values of the same call and
+ * sums the ranks' partials in rank order, so every rank writes the same y. No reference
+ * counterpart: the reference has no multi-GPU code.
+ *
+ * Set-up, once per group (every rank, same order): tf_peer_mailbox_alloc on each rank, share
+ * the IPC handles (e.g. an all-gather over the process group), tf_peer_mailbox_open the peers'
+ * handles, fill a TfPeerSet. Ranks must be on distinct GPUs. Every rank must then issue the same
+ * sequence of tf_w4a16_linear_allreduce calls (the mailbox counts calls on the device, so the
+ * calls may be captured in a CUDA graph and replayed). Peers must reach each call within 2 s of
+ * each other: a rank whose peer does not arrive in time records an error (read it with
+ * tf_peer_mailbox_error) and writes an incomplete sum. */
+#define TF_MAX_PEERS 8
+#define TF_IPC_HANDLE_BYTES 64
+
+typedef struct TfPeerSet {
+  int32_t rank;                    /* this process's rank in [0, world) */
+  int32_t world;                   /* 2..TF_MAX_PEERS */
+  int32_t max_m;                   /* mailbox capacity: tokens (<= 8) ... */
+  int32_t max_n;                   /* ... and output columns */
+  void* mailbox[TF_MAX_PEERS];     /* rank q's mailbox mapped in this process; [rank] is local */
+} TfPeerSet;
+
+/* Bytes of one rank's mailbox for (world, max_m, max_n). */
+TF_API size_t tf_peer_mailbox_bytes(int32_t world, int32_t max_m, int32_t max_n);
+/* cudaMalloc + zero fill of `bytes` on the current device; writes the device pointer and the
+ * TF_IPC_HANDLE_BYTES-byte IPC handle that peers open. */
+TF_API int tf_peer_mailbox_alloc(size_t bytes, void** mailbox, void* ipc_handle);
+/* Maps a peer's mailbox (cudaIpcOpenMemHandle) into this process. */
+TF_API int tf_peer_mailbox_open(const void* ipc_handle, void** mailbox);
+TF_API int tf_peer_mailbox_close(void* peer_mailbox);
+TF_API int tf_peer_mailbox_free(void* mailbox);
+/* Reads (*out_code: 0 = none) and clears the mailbox's error word (synchronous copy). */
+TF_API int tf_peer_mailbox_error(void* mailbox, int* out_code);
+
+/* y = sum over ranks of this rank's tf_w4a16_linear partial (bias given on one rank only).
+ * Decode sizes only (the GEMV plan without a second reduce launch); other shapes return
+ * TF_ERR_UNSUPPORTED and the caller uses tf_w4a16_linear plus a collective. */
+TF_API int tf_w4a16_linear_allreduce(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                    const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                    const uint16_t* bias, int64_t N, int32_t group_size,
+                    uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                    const TfPeerSet* peers, void* stream);
+
 /* Launch-table introspection (replaces config.default_config / GemmConfig, config.py:23-92).
  * Writes the launch chosen for (M, N, K, G) into out[0..8]:
  *   {kernel (0 = gemv, 1 = mma gemm, 2 = tcgen05 gemm), m_bucket, tile_n, warps_k, split_k,

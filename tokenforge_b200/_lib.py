@@ -61,12 +61,38 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P],
     ),
+    "tf_peer_mailbox_bytes": (_SZ, [_I32, _I32, _I32]),
+    "tf_peer_mailbox_alloc": (ctypes.c_int, [_SZ, _P, _P]),
+    "tf_peer_mailbox_open": (ctypes.c_int, [_P, _P]),
+    "tf_peer_mailbox_close": (ctypes.c_int, [_P]),
+    "tf_peer_mailbox_free": (ctypes.c_int, [_P]),
+    "tf_peer_mailbox_error": (ctypes.c_int, [_P, _P]),
+    "tf_w4a16_linear_allreduce": (
+        ctypes.c_int,
+        [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _SZ, _P, _P],
+    ),
     "tf_launch_plan": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P]),
     "tf_rmsnorm_fp8_quant": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _F32, _P, _P, _P, _P]),
     "tf_cast_e4m3": (ctypes.c_int, [_P, _I64, _P, _P]),
     "tf_device_error": (ctypes.c_int, [_P]),
     "tf_reset_device_error": (ctypes.c_int, []),
 }
+
+TF_MAX_PEERS = 8
+TF_IPC_HANDLE_BYTES = 64
+
+
+class TfPeerSet(ctypes.Structure):
+    """Mirror of ``TfPeerSet`` in include/tokenforge_b200.h."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("max_m", ctypes.c_int32),
+        ("max_n", ctypes.c_int32),
+        ("mailbox", ctypes.c_void_p * TF_MAX_PEERS),
+    ]
+
 
 _lock = threading.Lock()
 

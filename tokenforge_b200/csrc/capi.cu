@@ -7,6 +7,7 @@
 // given (M, N, K, G) always launches the same grid and produces bit-identical output.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "tf_common.cuh"
@@ -193,6 +194,14 @@ int run_linear(const LinearArgs& a, cudaStream_t stream, int force_kernel) {
     st = plan_mma(a.M, a.N, a.K, &pl);
     if (st != TF_OK) return st;
   }
+  if (a.peers != nullptr) {
+    // The fused all-reduce needs the single-launch GEMV plan, every CTA resident at once (peers
+    // wait on each other's tiles) and the mailbox capacity.
+    const int64_t ctas = static_cast<int64_t>(pl.grid_x) * pl.split_k;
+    if (pl.kernel != kKernelGemv || pl.split_k != pl.cluster || pl.cluster > 2 ||
+        ctas > 2 * kNumSms || a.M > a.peers->max_m || a.N > a.peers->max_n)
+      return TF_ERR_UNSUPPORTED;
+  }
   if (pl.workspace > 0 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace))
     return TF_ERR_WORKSPACE;
   if (pl.kernel == kKernelTcGemm) return launch_tc_gemm(pl, a, stream);
@@ -204,6 +213,7 @@ LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const
                      const uint16_t* scales, const int32_t* qzeros, const uint16_t* bias,
                      int64_t N, int32_t G, uint16_t* y, int64_t ldy, void* ws, size_t wsb) {
   LinearArgs a;
+  a.peers = nullptr;
   a.x = x;
   a.M = M;
   a.K = K;
@@ -346,6 +356,96 @@ int tf_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
   const auto a = tfb::make_args(x, M, K, ldx, qweight_t, scales, qzeros, bias, N, group_size, y,
                                 ldy, workspace, workspace_bytes);
   return tfb::run_linear(a, static_cast<cudaStream_t>(stream), -1);
+}
+
+size_t tf_peer_mailbox_bytes(int32_t world, int32_t max_m, int32_t max_n) {
+  if (world < 2 || world > TF_MAX_PEERS || max_m < 1 || max_m > 8 || max_n < 8) return 0;
+  return tfb::peer_layout(world, max_m, max_n).bytes;
+}
+
+int tf_peer_mailbox_alloc(size_t bytes, void** mailbox, void* ipc_handle) {
+  if (bytes == 0 || !mailbox || !ipc_handle) return TF_ERR_INVALID_ARG;
+  static_assert(sizeof(cudaIpcMemHandle_t) == TF_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    tfb::last_cuda_error() = static_cast<int>(e);
+    cudaGetLastError();
+    return TF_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *mailbox = p;
+  return TF_OK;
+}
+
+int tf_peer_mailbox_open(const void* ipc_handle, void** mailbox) {
+  if (!ipc_handle || !mailbox) return TF_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(mailbox, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    tfb::last_cuda_error() = static_cast<int>(e);
+    cudaGetLastError();
+    return TF_ERR_CUDA;
+  }
+  return TF_OK;
+}
+
+int tf_peer_mailbox_close(void* peer_mailbox) {
+  if (!peer_mailbox) return TF_ERR_INVALID_ARG;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_mailbox);
+  if (e != cudaSuccess) {
+    tfb::last_cuda_error() = static_cast<int>(e);
+    cudaGetLastError();
+    return TF_ERR_CUDA;
+  }
+  return TF_OK;
+}
+
+int tf_peer_mailbox_free(void* mailbox) {
+  if (!mailbox) return TF_ERR_INVALID_ARG;
+  const cudaError_t e = cudaFree(mailbox);
+  if (e != cudaSuccess) {
+    tfb::last_cuda_error() = static_cast<int>(e);
+    cudaGetLastError();
+    return TF_ERR_CUDA;
+  }
+  return TF_OK;
+}
+
+int tf_peer_mailbox_error(void* mailbox, int* out_code) {
+  if (!mailbox || !out_code) return TF_ERR_INVALID_ARG;
+  uint32_t* err = static_cast<uint32_t*>(mailbox) + 2;
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v != 0) e = cudaMemset(err, 0, sizeof(v));
+  if (e != cudaSuccess) {
+    tfb::last_cuda_error() = static_cast<int>(e);
+    cudaGetLastError();
+    return TF_ERR_CUDA;
+  }
+  *out_code = static_cast<int>(v);
+  return TF_OK;
+}
+
+int tf_w4a16_linear_allreduce(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                              const int32_t* qweight_t, const uint16_t* scales,
+                              const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                              int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
+                              size_t workspace_bytes, const TfPeerSet* peers, void* stream) {
+  if (!peers || peers->world < 2 || peers->world > TF_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world || peers->max_m < 1 || peers->max_m > 8 || peers->max_n < 8)
+    return TF_ERR_INVALID_ARG;
+  for (int q = 0; q < peers->world; ++q)
+    if (!peers->mailbox[q]) return TF_ERR_INVALID_ARG;
+  auto a = tfb::make_args(x, M, K, ldx, qweight_t, scales, qzeros, bias, N, group_size, y, ldy,
+                          workspace, workspace_bytes);
+  a.peers = peers;
+  return tfb::run_linear(a, static_cast<cudaStream_t>(stream), tfb::kKernelGemv);
 }
 
 int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/tokenforge_b200.h"
+
 namespace tfb {
 
 enum LinearKernel : int {
@@ -45,7 +47,21 @@ struct LinearArgs {
   int64_t ldy;
   void* workspace;
   size_t workspace_bytes;
+  const TfPeerSet* peers;  // row-parallel all-reduce through peer mailboxes (null: none)
 };
+
+// One rank's mailbox: a 256-byte header (u32 call counter, arrival counter, error word), then
+// per (call parity, source rank) a [max_m, max_n] array of 64-bit words, each an fp32 partial
+// in the low half and the tag of the call that wrote it in the high half.
+struct PeerLayout {
+  size_t data_off, bytes;
+};
+inline PeerLayout peer_layout(int world, int max_m, int max_n) {
+  PeerLayout l;
+  l.data_off = 256;
+  l.bytes = l.data_off + static_cast<size_t>(2) * world * max_m * max_n * 8;
+  return l;
+}
 
 int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 int launch_mma_tiles(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);

@@ -53,6 +53,12 @@ struct GemvParams {
   int bps;          // 128-wide K blocks per CTA
   int cluster;      // CTAs per cluster along the K split (1, 2, 4 or 8)
   int xs_stride;    // fp16 elements per staged activation row
+  // Row-parallel all-reduce through peer mailboxes (peer_world > 1; see peer_exchange).
+  int peer_rank, peer_world;
+  int peer_max_m, peer_max_n;
+  int peer_participants;                  // storing warps of the grid (one per 32-row tile)
+  uint32_t* peer_ctl;                     // own mailbox header: call counter, arrivals, error
+  uint64_t* peer_data[TF_MAX_PEERS];       // rank q's tagged partials [2][world][max_m][max_n]
 };
 
 // One K block of this lane's four rows, in registers from issue to use.
@@ -245,6 +251,128 @@ __device__ __forceinline__ void fold_grp(float (&y)[2][4], const float (&acc)[2]
   }
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint64_t ld_volatile_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+constexpr uint64_t kPeerWaitNs = 2000000000ull;  // give up on a silent peer after 2 s
+
+// Row-parallel all-reduce of one 32-row tile, run by the warp that holds the tile's final fp32
+// partial (v, fragment layout as in the store below; bias is passed on one rank only). Every
+// value travels as one 64-bit word (fp32 bits | call tag << 32) written with a single store into
+// slot [parity][me] of each peer's mailbox, so a reader that sees the tag also sees the value
+// (64-bit aligned stores are single-copy atomic): no fences or separate flags. Each lane then
+// polls its own values from every peer (bounded wait), sums the ranks' partials in rank order
+// (its own from registers), so all ranks write identical y, and the last storing warp of the
+// grid advances the call counter. Calls alternate between two parities; a rank cannot get two
+// calls ahead of a peer's reads, because finishing a call needs that peer's values of the call,
+// which the peer writes only after its previous call (and its reads) ended. Tags are call + 1.
+__device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (&v)[2][4], int rr,
+                                              int c, int lane, uint32_t call) {
+  const int W = p.peer_world, me = p.peer_rank;
+  const int par = static_cast<int>(call & 1u);
+  const uint32_t tag = call + 1u;
+  const size_t slot = static_cast<size_t>(p.peer_max_m) * p.peer_max_n;
+  float own[2][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+      own[t][r] = v[t][r];
+      if (n < p.N && m < p.M && p.bias) own[t][r] += __half2float(__ldg(p.bias + n));
+    }
+  for (int q = 0; q < W; ++q) {
+    if (q == me) continue;
+    uint64_t* d = p.peer_data[q] + (static_cast<size_t>(par) * W + me) * slot;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+        if (n < p.N && m < p.M)
+          st_volatile_u64(d + static_cast<size_t>(m) * p.peer_max_n + n,
+                          (static_cast<uint64_t>(tag) << 32) | __float_as_uint(own[t][r]));
+      }
+  }
+  // Sum in rank order. All of a peer's words for this lane are requested together (independent
+  // loads), and only those whose tag is not yet the call's are polled again.
+  const uint64_t* mine = p.peer_data[me] + static_cast<size_t>(par) * W * slot;
+  float sum[2][4];
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sum[t][r] = 0.f;
+  bool timed_out = false;
+  const uint64_t t0 = globaltimer_ns();
+  for (int q = 0; q < W; ++q) {
+    if (q == me) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sum[t][r] += own[t][r];
+      continue;
+    }
+    const uint64_t* src = mine + q * slot;
+    uint64_t w[2][4];
+    bool live[2][4];
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+        live[t][r] = n < p.N && m < p.M;
+        w[t][r] = live[t][r] ? ld_volatile_u64(src + static_cast<size_t>(m) * p.peer_max_n + n)
+                             : (static_cast<uint64_t>(tag) << 32);
+      }
+    while (true) {
+      bool pending = false;
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (static_cast<uint32_t>(w[t][r] >> 32) != tag) {
+            const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+            w[t][r] = ld_volatile_u64(src + static_cast<size_t>(m) * p.peer_max_n + n);
+            pending = true;
+          }
+      if (!pending || timed_out) break;
+      if (globaltimer_ns() - t0 > kPeerWaitNs) timed_out = true;
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) sum[t][r] += __uint_as_float(static_cast<uint32_t>(w[t][r]));
+  }
+#pragma unroll
+  for (int t = 0; t < 2; ++t)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+      if (n < p.N && m < p.M) p.y[m * p.ldy + n] = __float2half_rn(sum[t][r]);
+    }
+  if (timed_out) atomicCAS(p.peer_ctl + 2, 0u, 1u);
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(p.peer_ctl + 1, 1u) == static_cast<uint32_t>(p.peer_participants - 1)) {
+      atomicExch(p.peer_ctl + 1, 0u);
+      __threadfence();
+      atomicAdd(p.peer_ctl, 1u);
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -305,7 +433,13 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   };
   load(s0, b0);
   load(s1, b0 + 1);
+  // The next kernel on the stream may be scheduled once every CTA of this grid has passed this
+  // point (so all of them are running or done): its CTAs take SM slots as ours retire and issue
+  // their own weight loads early, and its griddepcontrol.wait still waits for this grid to end.
+  pdl_launch_dependents();
   pdl_wait();
+  // The peer call counter is read after the wait: the previous call on this stream has ended.
+  const uint32_t call = p.peer_world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.peer_ctl) : 0u;
 
   // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory.
   {
@@ -338,7 +472,6 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
     step(s1, b + 1);
     load(s1, b + 3);
   }
-  pdl_launch_dependents();
   if constexpr (kFact) {
     // A non-finite activation or scale makes some y non-finite (fp32 sums of finite fp16
     // products cannot overflow). Then the warp recomputes its range with the per-weight dequant
@@ -419,6 +552,10 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   // Fragment value r of tile t: row 4q + 2t (r < 2) or 4q + 2t + 1 (r >= 2), token 2c + (r & 1).
   const int split = static_cast<int>(blockIdx.y) / p.cluster;
   const bool direct = static_cast<int>(gridDim.y) == p.cluster;
+  if (p.peer_world > 1) {  // the host admits peers only for direct plans
+    peer_exchange(p, v, rr, L.c, lane, call);
+    return;
+  }
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
 #pragma unroll
@@ -531,6 +668,23 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   p.xs_stride = plan.blocks_per_split * kKB + 8;
   const int outer = plan.split_k / plan.cluster;  // splits reduced by the second kernel
   p.partial = outer > 1 ? static_cast<float*>(a.workspace) : nullptr;
+  p.peer_world = 0;
+  p.peer_rank = 0;
+  p.peer_ctl = nullptr;
+  if (a.peers != nullptr) {
+    const TfPeerSet& ps = *a.peers;
+    const PeerLayout lay = peer_layout(ps.world, ps.max_m, ps.max_n);
+    p.peer_world = ps.world;
+    p.peer_rank = ps.rank;
+    p.peer_max_m = ps.max_m;
+    p.peer_max_n = ps.max_n;
+    p.peer_participants = static_cast<int>(plan.grid_x) * (kCtaWarps / plan.warps_k);
+    p.peer_ctl = static_cast<uint32_t*>(ps.mailbox[ps.rank]);
+    for (int q = 0; q < TF_MAX_PEERS; ++q) {
+      char* base = q < ps.world ? static_cast<char*>(ps.mailbox[q]) : nullptr;
+      p.peer_data[q] = base ? reinterpret_cast<uint64_t*>(base + lay.data_off) : nullptr;
+    }
+  }
   const size_t smem = gemv_smem_bytes(a.M, plan.blocks_per_split);
   const bool pdl = (launch_flags() & TF_LAUNCH_PDL) != 0;
   // Group size 128 (one K block per group): the scale is applied once per block after the

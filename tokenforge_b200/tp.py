@@ -100,9 +100,141 @@ def shard_layer(
     raise ValueError(f"kind must be 'column' or 'row', got {kind!r}")
 
 
-def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None) -> torch.Tensor:  # type: ignore[no-untyped-def]
+class PeerMailbox:
+    """Per-rank mailboxes for the row-parallel all-reduce fused into the decode GEMV
+    (``tf_w4a16_linear_allreduce``): each rank allocates one, the IPC handles are all-gathered
+    over ``group`` and every peer's mailbox is mapped into this process. Collective: every rank
+    constructs it (and calls :meth:`close`) in the same order. Ranks must sit on distinct GPUs
+    (the kernels of different ranks wait on each other)."""
+
+    def __init__(self, group=None, max_m: int = 8, max_n: int = 65536,  # type: ignore[no-untyped-def]
+                 device: torch.device | None = None) -> None:
+        import ctypes
+
+        import torch.distributed as dist
+
+        from tokenforge_b200 import _lib
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if not 2 <= self.world <= _lib.TF_MAX_PEERS:
+            raise ValueError(f"peer all-reduce needs 2..{_lib.TF_MAX_PEERS} ranks, got {self.world}")
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        props = torch.cuda.get_device_properties(self.device)
+        ids: list[object] = [None] * self.world
+        dist.all_gather_object(ids, str(getattr(props, "uuid", self.device)), group=group)
+        if len(set(ids)) != self.world:
+            raise RuntimeError("peer all-reduce ranks must be on distinct GPUs")
+        lib = _lib.lib()
+        self.bytes = int(lib.tf_peer_mailbox_bytes(self.world, max_m, max_n))
+        if self.bytes == 0:
+            raise ValueError(f"bad mailbox shape: world={self.world} max_m={max_m} max_n={max_n}")
+        handle = (ctypes.c_char * _lib.TF_IPC_HANDLE_BYTES)()
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check("tf_peer_mailbox_alloc",
+                       lib.tf_peer_mailbox_alloc(self.bytes, ctypes.byref(own), handle))
+        handles: list[object] = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers = _lib.TfPeerSet()
+        self.peers.rank, self.peers.world = self.rank, self.world
+        self.peers.max_m, self.peers.max_n = max_m, max_n
+        self._opened: list[int] = []
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                if q == self.rank:
+                    self.peers.mailbox[q] = own.value
+                    continue
+                hq = (ctypes.c_char * _lib.TF_IPC_HANDLE_BYTES).from_buffer_copy(handles[q])  # type: ignore[arg-type]
+                mq = ctypes.c_void_p()
+                _lib.check("tf_peer_mailbox_open", lib.tf_peer_mailbox_open(hq, ctypes.byref(mq)))
+                self.peers.mailbox[q] = mq.value
+                self._opened.append(int(mq.value))  # type: ignore[arg-type]
+        self._own = int(own.value)  # type: ignore[arg-type]
+        dist.barrier(group=group)
+
+    def error(self) -> int:
+        """Device-side error word (1 = a peer wait gave up), cleared on read."""
+        import ctypes
+
+        from tokenforge_b200 import _lib
+
+        out = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _lib.check("tf_peer_mailbox_error",
+                       _lib.lib().tf_peer_mailbox_error(ctypes.c_void_p(self._own), ctypes.byref(out)))
+        return int(out.value)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        from tokenforge_b200 import _lib
+
+        if self._own == 0:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no peer still writes into our mailbox
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            for m in self._opened:
+                _lib.check("tf_peer_mailbox_close", lib.tf_peer_mailbox_close(m))
+            _lib.check("tf_peer_mailbox_free", lib.tf_peer_mailbox_free(self._own))
+        self._opened, self._own = [], 0
+
+    def supports(self, m: int, n: int, k: int, group_size: int) -> bool:
+        """Whether every rank's row shard of an ``[m, k] x [n, k]`` layer runs the fused kernel
+        (the same answer on all ranks, from the global shape alone, so that no rank waits for a
+        peer that took the unfused path)."""
+        from tokenforge_b200.config import launch_plan
+
+        if m > self.peers.max_m or n > self.peers.max_n:
+            return False
+        for k0, k1 in row_bounds(k, group_size, self.world):
+            try:
+                pl = launch_plan(m, n, k1 - k0, group_size)
+            except ValueError:
+                return False
+            if (pl.kernel != "gemv" or pl.split_k != pl.cluster or pl.cluster > 2
+                    or pl.grid_x * pl.split_k > 2 * 148):
+                return False
+        return True
+
+    def linear(self, x: torch.Tensor, w: W4A16Weights, bias: torch.Tensor | None) -> torch.Tensor | None:
+        """Fused decode GEMV + all-reduce of this rank's row shard; None when the shape is not
+        served by the fused kernel (the caller then uses the plain linear + a collective)."""
+        import ctypes
+
+        from tokenforge_b200 import _lib
+        from tokenforge_b200.ops import _aligned_rows, _check_inputs, _require
+
+        m, n, k = _check_inputs(x, w.qweight_t, w.scales, w.qzeros, w.group_size)
+        for name, t in (("x", x), ("qweight_t", w.qweight_t), ("scales", w.scales),
+                        ("qzeros", w.qzeros)):
+            _require(t, name)
+        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+        x = _aligned_rows(x)
+        lib = _lib.lib()
+        wsb = int(lib.tf_w4a16_workspace_bytes(m, n, k, w.group_size))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=x.device) if wsb else None
+        with torch.cuda.device(x.device):
+            status = lib.tf_w4a16_linear_allreduce(
+                x.data_ptr(), m, k, x.stride(0), w.qweight_t.data_ptr(), w.scales.data_ptr(),
+                w.qzeros.data_ptr(), _lib.ptr(None if bias is None else bias.contiguous()), n,
+                w.group_size, y.data_ptr(), n, _lib.ptr(ws), wsb, ctypes.byref(self.peers),
+                _lib.stream_ptr(x.device))
+        if status == _lib.TF_ERR_UNSUPPORTED:
+            return None
+        _lib.check("tf_w4a16_linear_allreduce", status)
+        return y
+
+
+def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None,  # type: ignore[no-untyped-def]
+                 peers: PeerMailbox | None = None) -> torch.Tensor:
     """Run one rank's shard. Column-parallel returns this rank's columns; row-parallel takes
-    the full activations, uses its K slice, and all-reduces the fp16 partials in place.
+    the full activations, uses its K slice, and sums the ranks' partials: through ``peers``
+    (the all-reduce fused into the decode GEMV) when given and the shape allows it, else with
+    an all-reduce of the fp16 partials over ``group``.
 
     ``linear(x, weights, bias) -> fp16 [M, N]`` computes the local product; by default the
     kernel library's launch table (GEMV for M <= 8, tensor-core GEMM above)."""
@@ -118,6 +250,11 @@ def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None) ->
     if shard.kind == "column":
         return linear(x, w, shard.bias)
     k0, k1 = shard.bounds
+    if peers is not None and peers.supports(x.shape[0], w.n, x.shape[1], w.group_size):
+        fused = peers.linear(x[:, k0:k1], w, shard.bias)
+        if fused is None:
+            raise RuntimeError("fused all-reduce refused a shape its plan check admitted")
+        return fused
     y = linear(x[:, k0:k1], w, shard.bias)
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
