@@ -305,61 +305,93 @@ __device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (
                           (static_cast<uint64_t>(tag) << 32) | __float_as_uint(own[t][r]));
       }
   }
-  // Sum in rank order. All of a peer's words for this lane are requested together (independent
-  // loads), and only those whose tag is not yet the call's are polled again.
+  // Sum in rank order. Words are requested in batches of independent loads (all of the lane's
+  // words of the one peer when world == 2; else, per tile, the words of all peers), so a batch
+  // costs one round trip; only words whose tag is not yet the call's are polled again.
   const uint64_t* mine = p.peer_data[me] + static_cast<size_t>(par) * W * slot;
-  float sum[2][4];
+  bool timed_out = false;
+  const uint64_t t0 = globaltimer_ns();
+  size_t off[2][4];
+  bool live[2][4];
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
-    for (int r = 0; r < 4; ++r) sum[t][r] = 0.f;
-  bool timed_out = false;
-  const uint64_t t0 = globaltimer_ns();
-  for (int q = 0; q < W; ++q) {
-    if (q == me) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) sum[t][r] += own[t][r];
-      continue;
+    for (int r = 0; r < 4; ++r) {
+      const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
+      live[t][r] = n < p.N && m < p.M;
+      off[t][r] = static_cast<size_t>(m) * p.peer_max_n + n;
     }
-    const uint64_t* src = mine + q * slot;
+  auto poll = [&](uint64_t& w, const uint64_t* src) {
+    if (static_cast<uint32_t>(w >> 32) != tag) {
+      w = ld_volatile_u64(src);
+      return true;
+    }
+    return false;
+  };
+  float sum[2][4];
+  if (W == 2) {
+    const int q = 1 - me;
     uint64_t w[2][4];
-    bool live[2][4];
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
-        live[t][r] = n < p.N && m < p.M;
-        w[t][r] = live[t][r] ? ld_volatile_u64(src + static_cast<size_t>(m) * p.peer_max_n + n)
+      for (int r = 0; r < 4; ++r)
+        w[t][r] = live[t][r] ? ld_volatile_u64(mine + q * slot + off[t][r])
                              : (static_cast<uint64_t>(tag) << 32);
-      }
     while (true) {
       bool pending = false;
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
-          if (static_cast<uint32_t>(w[t][r] >> 32) != tag) {
-            const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
-            w[t][r] = ld_volatile_u64(src + static_cast<size_t>(m) * p.peer_max_n + n);
-            pending = true;
-          }
+        for (int r = 0; r < 4; ++r) pending |= poll(w[t][r], mine + q * slot + off[t][r]);
       if (!pending || timed_out) break;
       if (globaltimer_ns() - t0 > kPeerWaitNs) timed_out = true;
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) sum[t][r] += __uint_as_float(static_cast<uint32_t>(w[t][r]));
+      for (int r = 0; r < 4; ++r) {
+        const float other = __uint_as_float(static_cast<uint32_t>(w[t][r]));
+        sum[t][r] = me == 0 ? own[t][r] + other : other + own[t][r];
+      }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      uint64_t w[TF_MAX_PEERS][4];
+#pragma unroll
+      for (int q = 0; q < TF_MAX_PEERS; ++q)
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          w[q][r] = (q < W && q != me && live[t][r])
+                        ? ld_volatile_u64(mine + q * slot + off[t][r])
+                        : (static_cast<uint64_t>(tag) << 32);
+      while (true) {
+        bool pending = false;
+#pragma unroll
+        for (int q = 0; q < TF_MAX_PEERS; ++q)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) pending |= poll(w[q][r], mine + q * slot + off[t][r]);
+        if (!pending || timed_out) break;
+        if (globaltimer_ns() - t0 > kPeerWaitNs) timed_out = true;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < TF_MAX_PEERS; ++q) {
+          if (q >= W) break;
+          acc += (q == me) ? own[t][r] : __uint_as_float(static_cast<uint32_t>(w[q][r]));
+        }
+        sum[t][r] = acc;
+      }
+    }
   }
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
-      if (n < p.N && m < p.M) p.y[m * p.ldy + n] = __float2half_rn(sum[t][r]);
+      if (live[t][r]) p.y[m * p.ldy + n] = __float2half_rn(sum[t][r]);
     }
   if (timed_out) atomicCAS(p.peer_ctl + 2, 0u, 1u);
   __syncwarp();
