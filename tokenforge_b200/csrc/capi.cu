@@ -42,8 +42,8 @@ constexpr BucketEntry kTable[] = {
     {4096, kKernelTcGemm, 256}, {1 << 30, kKernelTcGemm, 256},
 };
 
-// Decode GEMV: 32-row warp tiles over 128-wide K blocks, K split over WARPS_K warps of a CTA and
-// over the C CTAs of a cluster. (WARPS_K, C) is the pair that brings the CTA count closest to two
+// Decode GEMV: 32-row warp tiles over 128-wide K blocks, K split over WARPS_K warps of an 8-warp
+// CTA and over the C CTAs of a cluster. (WARPS_K, C) is the pair that brings the CTA count closest to two
 // per SM without exceeding it (ties: fewer warps per tile, then smaller clusters), keeping at least
 // one block per warp. C grows further if the CTA's staged activations would exceed 100 KB of
 // shared memory; beyond clusters of 8, K is also split across clusters (fp32 partials + reduce).
@@ -78,12 +78,22 @@ int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   const int64_t per = cdiv(kblocks, splits);
   splits = cdiv(kblocks, per);
   if (splits % cluster != 0) splits = cdiv(splits, cluster) * cluster;  // whole clusters
-  const int64_t gx = cdiv(n_tiles, 8 / best_wk);
+  // A cluster of two 8-warp CTAs that each take one row tile is one 16-warp CTA (one per SM)
+  // splitting K 16 ways: same warps, but the split is summed in shared memory instead of
+  // through two cluster barriers (about 1 us per launch). Its staged activations may use most
+  // of the SM's shared memory.
+  if (best_wk == 8 && cluster == 2 && splits == 2 && x_bytes(1) <= 200 * 1024) {
+    best_wk = 16;
+    cluster = 1;
+    splits = 1;
+  }
+  const int64_t per_split = cdiv(kblocks, splits);
+  const int64_t gx = cdiv(n_tiles, gemv_warps_n(best_wk));
   if (gx > 0x7fffffffLL || splits > 65535) return TF_ERR_UNSUPPORTED;
   pl->warps_k = best_wk;
   pl->cluster = cluster;
   pl->split_k = static_cast<int>(splits);
-  pl->blocks_per_split = static_cast<int>(per);
+  pl->blocks_per_split = static_cast<int>(per_split);
   pl->grid_x = static_cast<unsigned>(gx);
   pl->grid_y = static_cast<unsigned>(splits);
   pl->grid_z = 1;
@@ -198,8 +208,9 @@ int run_linear(const LinearArgs& a, cudaStream_t stream, int force_kernel) {
     // The fused all-reduce needs the single-launch GEMV plan, every CTA resident at once (peers
     // wait on each other's tiles) and the mailbox capacity.
     const int64_t ctas = static_cast<int64_t>(pl.grid_x) * pl.split_k;
+    const int64_t resident = pl.warps_k >= 16 ? kNumSms : 2 * kNumSms;
     if (pl.kernel != kKernelGemv || pl.split_k != pl.cluster || pl.cluster > 2 ||
-        ctas > 2 * kNumSms || a.M > a.peers->max_m || a.N > a.peers->max_n)
+        ctas > resident || a.M > a.peers->max_m || a.N > a.peers->max_n)
       return TF_ERR_UNSUPPORTED;
   }
   if (pl.workspace > 0 && (a.workspace == nullptr || a.workspace_bytes < pl.workspace))

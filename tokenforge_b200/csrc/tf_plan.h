@@ -65,6 +65,9 @@ inline PeerLayout peer_layout(int world, int max_m, int max_n) {
 
 int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
 int launch_mma_tiles(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);
+// Row tiles (32 weight rows each) per decode-GEMV CTA for a plan's warps_k: CTAs are 8 warps
+// (two per SM) with warps_k <= 8, or one 16-warp CTA per SM with warps_k == 16.
+inline int gemv_warps_n(int warps_k) { return warps_k >= 16 ? 1 : 8 / warps_k; }
 // Dynamic shared memory of the decode GEMV: M staged activation rows of bps * 128 (+8) fp16.
 size_t gemv_smem_bytes(int64_t M, int bps);
 int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream);

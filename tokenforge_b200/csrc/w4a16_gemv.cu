@@ -35,7 +35,8 @@ namespace tfb {
 namespace {
 
 constexpr int kKB = 128;         // K values per block
-constexpr int kCtaWarps = 8;     // warps per CTA (WARPS_N x WARPS_K)
+constexpr int kCtaWarps = 8;     // warps per CTA (WARPS_N x WARPS_K), two CTAs per SM ...
+constexpr int kWideWarps = 16;   // ... or one 16-warp CTA per SM splitting K 16 ways
 constexpr int kWarpRows = 32;    // weight rows per warp tile
 
 struct GemvParams {
@@ -424,11 +425,13 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
 }
 
 template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact>
-__global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const GemvParams p) {
-  static_assert(WARPS_N * WARPS_K == kCtaWarps, "CTA shape");
+__global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N * WARPS_K))
+    w4a16_gemv_kernel(const GemvParams p) {
+  constexpr int kWarps = WARPS_N * WARPS_K;
+  static_assert(kWarps == kCtaWarps || kWarps == kWideWarps, "CTA shape");
   extern __shared__ uint4 xs_smem[];
   // Per warp: two tiles x four fragment values x 32 lanes.
-  __shared__ float red[kCtaWarps * 2 * 4 * 32];
+  __shared__ float red[kWarps * 2 * 4 * 32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wn = warp / WARPS_K, wk = warp % WARPS_K;
@@ -473,7 +476,8 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
   // The peer call counter is read after the wait: the previous call on this stream has ended.
   const uint32_t call = p.peer_world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.peer_ctl) : 0u;
 
-  // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory.
+  // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory: every 16-byte piece is an
+  // asynchronous copy, all in flight together, so staging costs one L2 round trip.
   {
     const int vec_per_row = (kb1 - L.kb0) * (kKB / 8);
     const int total = p.M * vec_per_row;
@@ -481,9 +485,17 @@ __global__ void __launch_bounds__(32 * kCtaWarps, 2) w4a16_gemv_kernel(const Gem
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
       const int m = i / vec_per_row, v = i - m * vec_per_row;
       const int k = k_lo + 8 * v;
-      const uint4 val = k < p.K ? ldg_v4(p.x + m * p.ldx + k) : zero4();
-      xs_smem[(m * p.xs_stride) / 8 + v] = val;
+      uint4* dst = xs_smem + (m * p.xs_stride) / 8 + v;
+      if (k < p.K) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                     "l"(p.x + m * p.ldx + k)
+                     : "memory");
+      } else {
+        *dst = zero4();
+      }
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
   }
   __syncthreads();
 
@@ -625,7 +637,10 @@ template <int WN, int WK, bool kCluster, bool kFact>
 int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
                         cudaStream_t stream, bool pdl) {
   auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact>;
-  if (smem > 48 * 1024) {
+  // Static (the reduction buffer, 1 KB per warp) plus dynamic shared memory above the default
+  // 48 KB needs the opt-in limit raised.
+  constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 4 * 32 * sizeof(float);
+  if (smem + kStaticSmem > 48 * 1024) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) {
@@ -635,7 +650,7 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid_x, plan.grid_y, 1);
-  cfg.blockDim = dim3(32 * kCtaWarps);
+  cfg.blockDim = dim3(32 * WN * WK);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -670,6 +685,9 @@ int launch_gemv_shape(const LinearPlan& plan, const GemvParams& p, size_t smem, 
     case 2: return launch_gemv_variant<4, 2, kCluster, kFact>(plan, p, smem, st, pdl);
     case 4: return launch_gemv_variant<2, 4, kCluster, kFact>(plan, p, smem, st, pdl);
     case 8: return launch_gemv_variant<1, 8, kCluster, kFact>(plan, p, smem, st, pdl);
+    case 16:
+      if constexpr (kCluster) return TF_ERR_INVALID_ARG;
+      else return launch_gemv_variant<1, 16, false, kFact>(plan, p, smem, st, pdl);
     default: return TF_ERR_INVALID_ARG;
   }
 }
@@ -710,7 +728,7 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
     p.peer_rank = ps.rank;
     p.peer_max_m = ps.max_m;
     p.peer_max_n = ps.max_n;
-    p.peer_participants = static_cast<int>(plan.grid_x) * (kCtaWarps / plan.warps_k);
+    p.peer_participants = static_cast<int>(plan.grid_x) * gemv_warps_n(plan.warps_k);
     p.peer_ctl = static_cast<uint32_t*>(ps.mailbox[ps.rank]);
     for (int q = 0; q < TF_MAX_PEERS; ++q) {
       char* base = q < ps.world ? static_cast<char*>(ps.mailbox[q]) : nullptr;
