@@ -156,6 +156,23 @@ TF_API int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int6
                     const uint16_t* bias, int64_t N, int32_t group_size,
                     uint16_t* y, int64_t ldy, void* stream);
 
+/* ------------------------------------------------------------------ FP8 activations
+ * W4A16 linear fed by rmsnorm_fp8_quant's output: x[m, k] = e4m3(xq[m, k]) * x_scale[m *
+ * scale_stride] (scale_stride 1: the per-token fp32 scales, 0: one static scale), y as
+ * tf_w4a16_linear. No reference counterpart: the reference produces e4m3 activations but has no
+ * consumer for them (BASELINE config 4's block stack needs one).
+ * M <= 8 (decode GEMV): the codes are staged as their exact fp16 values and y is scaled in fp32
+ * before the bias, so the result is as accurate as with fp16 activations x.
+ * M > 8: x16 = fp16(e4m3 * scale) (one rounding) is written to the workspace, then the regular
+ * launch table runs on it. Workspace: tf_w4a16_fp8_workspace_bytes(M, N, K, group_size).
+ * xq must be 8-byte aligned with ldx (bytes) % 8 == 0. */
+TF_API size_t tf_w4a16_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_size);
+TF_API int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t scale_stride,
+                    int64_t M, int64_t K, int64_t ldx, const int32_t* qweight_t,
+                    const uint16_t* scales, const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                    int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------- row-parallel all-reduce over NVLink
  * Tensor-parallel o / down layers (row-split K) end in a sum of every rank's fp16 partial
  * (NCCL all-reduce after o and down). tf_w4a16_linear_allreduce fuses that

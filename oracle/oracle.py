@@ -35,6 +35,8 @@ _SIG = {
     "oracle_w4a16_ref_f64": (None, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P]),
     "oracle_w4a16_cpu_f32": (None, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P, _P, _I64]),
     "oracle_e4m3": (ctypes.c_uint8, [ctypes.c_float]),
+    "oracle_e4m3_value": (ctypes.c_double, [ctypes.c_uint8]),
+    "oracle_w4a16_ref_fp8_f64": (None, [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _P]),
     "oracle_rmsnorm_fp8": (None, [_P, _I64, _I64, _P, ctypes.c_float, _P, _P, _P]),
 }
 
@@ -179,6 +181,31 @@ def e4m3_codes(values: torch.Tensor) -> torch.Tensor:
     v = values.detach().cpu().to(torch.float32).reshape(-1).tolist()
     f = _lib().oracle_e4m3
     return torch.tensor([f(x) for x in v], dtype=torch.uint8).reshape(values.shape)
+
+
+def e4m3_values(codes: torch.Tensor) -> torch.Tensor:
+    """Values of e4m3fn codes (uint8) as fp64, decoded from the format's bit fields."""
+    f = _lib().oracle_e4m3_value
+    c = codes.detach().cpu().to(torch.uint8).reshape(-1).tolist()
+    return torch.tensor([f(v) for v in c], dtype=torch.float64).reshape(codes.shape)
+
+
+def w4a16_reference_fp8(xq: torch.Tensor, x_scale: torch.Tensor, qweight_t: torch.Tensor,
+                        scales: torch.Tensor, qzeros: torch.Tensor, group_size: int,
+                        bias: torch.Tensor | None = None) -> torch.Tensor:
+    """FP8-activation linear in fp64: (e4m3(xq) * x_scale) @ dequant(W)^T + bias. x_scale holds
+    one fp32 value per token ([M] or [M, 1]) or a single static value."""
+    q8 = _np(xq.reshape(-1, xq.shape[-1]), np.uint8)
+    sc = _np(x_scale.reshape(-1).to(torch.float32), np.float32)
+    stride = 0 if sc.size == 1 else 1
+    q, s, z = _np(qweight_t, np.int32), _np(scales, np.uint16), _np(qzeros, np.int32)
+    b = None if bias is None else _np(bias, np.uint16)
+    m, k = q8.shape
+    n = q.shape[0]
+    out = np.empty((m, n), dtype=np.float64)
+    _lib().oracle_w4a16_ref_fp8_f64(_addr(q8), _addr(sc), stride, m, k, _addr(q), _addr(s),
+                                    _addr(z), _addr(b), n, group_size, _addr(out))
+    return torch.from_numpy(out)
 
 
 def rmsnorm_fp8(x: torch.Tensor, weight: torch.Tensor, eps: float,

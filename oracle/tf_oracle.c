@@ -162,6 +162,37 @@ uint8_t oracle_e4m3(float v) {
   return (uint8_t)(sign | (biased << 3) | mant);
 }
 
+/* Value of an e4m3fn code (the inverse of oracle_e4m3 on its range): 1 sign bit, 4 exponent
+ * bits with bias 7, 3 mantissa bits; exponent 0 is subnormal (mantissa * 2^-9); code 0x7F /
+ * 0xFF is NaN; there are no infinities. This is the format torch.float8_e4m3fn decodes. */
+double oracle_e4m3_value(uint8_t c) {
+  const int sign = c >> 7, e = (c >> 3) & 0xF, mant = c & 0x7;
+  if (e == 0xF && mant == 0x7) return NAN;
+  const double mag = e == 0 ? ldexp((double)mant, -9) : ldexp(1.0 + mant / 8.0, e - 7);
+  return sign ? -mag : mag;
+}
+
+/* The FP8-activation linear (the consumer of rmsnorm_fp8_quant's (q, scale) that the reference
+ * lacks): y[m, n] = sum_k e4m3(xq[m, k]) * x_scale[m * stride] * w[n, k] + bias[n] in fp64,
+ * w the reference dequant (pack.py:189-194). xq [M, K] codes, row stride K. */
+void oracle_w4a16_ref_fp8_f64(const uint8_t* xq, const float* x_scale, int64_t stride, int64_t M,
+                              int64_t K, const int32_t* qweight_t, const uint16_t* scales,
+                              const int32_t* qzeros, const uint16_t* bias, int64_t N, int64_t G,
+                              double* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    for (int64_t m = 0; m < M; ++m) {
+      const double s = (double)x_scale[m * stride];
+      double acc = 0.0;
+      for (int64_t k = 0; k < K; ++k)
+        acc += oracle_e4m3_value(xq[m * K + k]) * s *
+               (double)tf_weight(qweight_t, scales, qzeros, N, K, G, n, k);
+      if (bias) acc += (double)h_from_bits(bias[n]);
+      out[m * N + n] = acc;
+    }
+  }
+}
+
 /* RMSNorm + e4m3 quantization (reference.py:35-56 for the rule; triton/rmsnorm_fp8.py:57-73
  * for the exact fp32 operations: IEEE sqrt and divisions). The sum of squares is accumulated
  * in fp64 and rounded once to fp32, so it does not depend on the summation order.

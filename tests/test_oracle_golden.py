@@ -150,3 +150,15 @@ def test_e4m3_rounding_kat() -> None:
     d = _load("e4m3_kat")
     codes = oracle.e4m3_codes(torch.from_numpy(d["probe"]))
     assert np.array_equal(codes.numpy(), d["codes"])
+
+
+def test_e4m3_decode_matches_torch_for_every_code() -> None:
+    """The oracle's e4m3fn decoder (used by the FP8-activation linear's reference) agrees with
+    torch.float8_e4m3fn, the arithmetic the reference's FP8 rule is written in."""
+    codes = torch.arange(256, dtype=torch.uint8)
+    got = oracle.e4m3_values(codes)
+    want = codes.view(torch.float8_e4m3fn).to(torch.float64)
+    assert bool(((got == want) | (got.isnan() & want.isnan())).all())
+    # and the encoder inverts it on every finite code
+    finite = ~want.isnan()
+    assert torch.equal(oracle.e4m3_codes(want[finite].float()), codes[finite])

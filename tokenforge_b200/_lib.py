@@ -61,6 +61,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P],
     ),
+    "tf_w4a16_fp8_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
+    "tf_w4a16_linear_fp8": (
+        ctypes.c_int,
+        [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _SZ, _P],
+    ),
     "tf_peer_mailbox_bytes": (_SZ, [_I32, _I32, _I32]),
     "tf_peer_mailbox_alloc": (ctypes.c_int, [_SZ, _P, _P]),
     "tf_peer_mailbox_open": (ctypes.c_int, [_P, _P]),

@@ -175,7 +175,10 @@ int validate_linear(const LinearArgs& a) {
   if (a.ldx < a.K || a.ldy < a.N) return TF_ERR_INVALID_ARG;
   if (a.M == 0) return TF_OK;
   if (!a.x || !a.qw || !a.scales || !a.qzeros || !a.y) return TF_ERR_INVALID_ARG;
-  if (!aligned16(a.x) || a.ldx % 8 != 0 || !aligned16(a.qw)) return TF_ERR_ALIGNMENT;
+  // fp16 activations are read 16 bytes at a time, e4m3 codes 8 bytes at a time.
+  const uintptr_t x_align = a.x8 != nullptr ? 8 : 16;
+  if (reinterpret_cast<uintptr_t>(a.x) % x_align != 0 || a.ldx % 8 != 0 || !aligned16(a.qw))
+    return TF_ERR_ALIGNMENT;
   return TF_OK;
 }
 
@@ -225,6 +228,9 @@ LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const
                      int64_t N, int32_t G, uint16_t* y, int64_t ldy, void* ws, size_t wsb) {
   LinearArgs a;
   a.peers = nullptr;
+  a.x8 = nullptr;
+  a.x_scale = nullptr;
+  a.x_scale_stride = 0;
   a.x = x;
   a.M = M;
   a.K = K;
@@ -457,6 +463,55 @@ int tf_w4a16_linear_allreduce(const uint16_t* x, int64_t M, int64_t K, int64_t l
                           workspace, workspace_bytes);
   a.peers = peers;
   return tfb::run_linear(a, static_cast<cudaStream_t>(stream), tfb::kKernelGemv);
+}
+
+size_t tf_w4a16_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_size) {
+  if (M < 1 || K < 1) return 0;
+  const size_t lin = tf_w4a16_workspace_bytes(M, N, K, group_size);
+  if (M <= 8) return lin;
+  const size_t x16 = (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256;
+  return x16 + lin;
+}
+
+int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t scale_stride, int64_t M,
+                        int64_t K, int64_t ldx, const int32_t* qweight_t, const uint16_t* scales,
+                        const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                        int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
+                        size_t workspace_bytes, void* stream_) {
+  using namespace tfb;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (scale_stride != 0 && scale_stride != 1) return TF_ERR_INVALID_ARG;
+  if (M < 0 || K < 1 || ldx < K) return TF_ERR_INVALID_ARG;
+  if (M == 0) return TF_OK;
+  if (!xq || !x_scale) return TF_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(xq) % 8 != 0 || ldx % 8 != 0) return TF_ERR_ALIGNMENT;
+  LinearPlan pl;
+  int st = plan_linear(M, N, K, group_size, &pl);
+  if (st != TF_OK) return st;
+  if (pl.kernel == kKernelGemv && gemv_fits(M, N, K, K, group_size) && M * ldx < (int64_t(1) << 31)) {
+    // Decode: the GEMV stages the codes exactly and scales y in fp32.
+    auto a = make_args(reinterpret_cast<const uint16_t*>(xq), M, K, K, qweight_t, scales, qzeros,
+                       bias, N, group_size, y, ldy, workspace, workspace_bytes);
+    a.ldx = ldx;
+    a.x8 = xq;
+    a.x_scale = x_scale;
+    a.x_scale_stride = scale_stride;
+    st = validate_linear(a);
+    if (st != TF_OK) return st;
+    if (pl.workspace > 0 && (workspace == nullptr || workspace_bytes < pl.workspace))
+      return TF_ERR_WORKSPACE;
+    return launch_gemv(pl, a, stream);
+  }
+  // Prefill: x16 = fp16(e4m3 * scale) in the workspace, then the regular launch table.
+  const size_t x16_bytes = (static_cast<size_t>(M) * K * 2 + 255) / 256 * 256;
+  if (workspace == nullptr || workspace_bytes < x16_bytes) return TF_ERR_WORKSPACE;
+  uint16_t* x16 = static_cast<uint16_t*>(workspace);
+  st = launch_fp8_to_fp16(xq, M, K, ldx, x_scale, scale_stride, x16, K, stream);
+  if (st != TF_OK) return st;
+  const auto a = make_args(x16, M, K, K, qweight_t, scales, qzeros, bias, N, group_size, y, ldy,
+                           static_cast<char*>(workspace) + x16_bytes,
+                           workspace_bytes - x16_bytes);
+  return run_linear(a, stream, -1);
 }
 
 int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,

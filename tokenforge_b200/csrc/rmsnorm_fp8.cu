@@ -16,6 +16,7 @@
 // shared memory. Generic path (any H, any alignment, H > 4096): one CTA per row, three sweeps
 // over the row (the second and third hit L2).
 #include "tf_common.cuh"
+#include "tf_plan.h"
 
 namespace tfb {
 namespace {
@@ -180,7 +181,40 @@ __global__ void cast_e4m3_kernel(const float* __restrict__ in, int64_t n, uint8_
   if (i < n) out[i] = static_cast<uint8_t>(cvt_e4m3x2(in[i], 0.f) & 0xFFu);
 }
 
+// x16[m, k] = fp16(e4m3(q[m, k]) * scale[m * stride]): the e4m3 value is exact in fp32, the
+// product is rounded once to fp16. One thread per 8 codes.
+__global__ void fp8_to_fp16_kernel(const uint8_t* __restrict__ q, int64_t M, int64_t K,
+                                   int64_t ldq, const float* __restrict__ scale, int64_t stride,
+                                   __half* __restrict__ x16, int64_t ldx16) {
+  const int64_t per_row = (K + 7) / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * per_row) return;
+  const int64_t m = i / per_row, k0 = (i - m * per_row) * 8;
+  const float s = scale[m * stride];
+  const uint8_t* src = q + m * ldq + k0;
+  __half* dst = x16 + m * ldx16 + k0;
+  for (int e = 0; e < 8 && k0 + e < K; e += 2) {
+    const uint16_t pair = (k0 + e + 1 < K) ? static_cast<uint16_t>(src[e] | (src[e + 1] << 8))
+                                           : static_cast<uint16_t>(src[e]);
+    uint32_t h;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(pair));
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    dst[e] = __float2half_rn(__fmul_rn(f.x, s));
+    if (k0 + e + 1 < K) dst[e + 1] = __float2half_rn(__fmul_rn(f.y, s));
+  }
+}
+
 }  // namespace
+
+int launch_fp8_to_fp16(const uint8_t* xq, int64_t M, int64_t K, int64_t ldq, const float* scale,
+                       int64_t stride, uint16_t* x16, int64_t ldx16, cudaStream_t stream) {
+  const int64_t n = M * ((K + 7) / 8);
+  if (n == 0) return TF_OK;
+  fp8_to_fp16_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, stream>>>(
+      xq, M, K, ldq, scale, stride, reinterpret_cast<__half*>(x16), ldx16);
+  return check_launch();
+}
+
 }  // namespace tfb
 
 extern "C" int tf_rmsnorm_fp8_quant(const uint16_t* x, int64_t T, int64_t H, int64_t ldx,

@@ -48,6 +48,11 @@ struct LinearArgs {
   void* workspace;
   size_t workspace_bytes;
   const TfPeerSet* peers;  // row-parallel all-reduce through peer mailboxes (null: none)
+  // FP8 activations for the decode GEMV (x8 != null replaces x): e4m3 codes, row stride ldx
+  // bytes, and the fp32 scale(s) multiplied into y before the bias.
+  const uint8_t* x8;
+  const float* x_scale;
+  int64_t x_scale_stride;
 };
 
 // One rank's mailbox: a 256-byte header (u32 call counter, arrival counter, error word), then
@@ -74,6 +79,9 @@ int launch_tc_gemm(const LinearPlan& plan, const LinearArgs& a, cudaStream_t str
 bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size);
 // Fills split_k / blocks_per_split / grid / workspace of a tensor-core plan whose tile_m is set.
 void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* plan);
+// x16[m, k] = fp16(e4m3(xq[m, k]) * scale[m * stride]) (one rounding), row stride ldx16.
+int launch_fp8_to_fp16(const uint8_t* xq, int64_t M, int64_t K, int64_t ldq, const float* scale,
+                       int64_t stride, uint16_t* x16, int64_t ldx16, cudaStream_t stream);
 // y[m, n] = fp16(sum_s partial[s, m, n] + bias[n]), splits summed in order 0..split-1.
 int launch_splitk_reduce(const float* partial, int split, int64_t M, int64_t N,
                          const uint16_t* bias, uint16_t* y, int64_t ldy, cudaStream_t stream);

@@ -42,6 +42,12 @@ constexpr int kWarpRows = 32;    // weight rows per warp tile
 struct GemvParams {
   const __half* x;
   int64_t ldx;
+  // FP8 activations (x8 != null, x unused): e4m3 codes [M, K] with row stride ldx bytes, staged
+  // as their exact fp16 values; y is multiplied by x_scale[m * x_scale_stride] in fp32 before
+  // the bias (stride 1: per-token scales, 0: one static scale).
+  const uint8_t* x8;
+  const float* x_scale;
+  int x_scale_stride;
   const int32_t* qw;
   const __half* scales;
   const int32_t* qzeros;
@@ -482,6 +488,39 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
     const int vec_per_row = (kb1 - L.kb0) * (kKB / 8);
     const int total = p.M * vec_per_row;
     const int k_lo = L.kb0 * kKB;
+    if (p.x8 != nullptr) {
+      // e4m3 codes: 8 bytes per 16-byte fp16 vector, converted exactly (every e4m3 value is an
+      // fp16 value; NaN stays NaN). Two loads per thread are in flight before the stores.
+      for (int i0 = threadIdx.x; i0 < total; i0 += 2 * blockDim.x) {
+        uint2 raw[2];
+        int idx[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = i0 + u * static_cast<int>(blockDim.x);
+          idx[u] = i;
+          raw[u] = make_uint2(0u, 0u);
+          if (i < total) {
+            const int m = i / vec_per_row, v = i - m * vec_per_row;
+            const int k = k_lo + 8 * v;
+            if (k < p.K) raw[u] = __ldg(reinterpret_cast<const uint2*>(p.x8 + m * p.ldx + k));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = idx[u];
+          if (i >= total) continue;
+          const int m = i / vec_per_row, v = i - m * vec_per_row;
+          const uint32_t w[2] = {raw[u].x, raw[u].y};
+          uint32_t h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint16_t pair = static_cast<uint16_t>(w[e >> 1] >> (16 * (e & 1)));
+            asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h[e]) : "h"(pair));
+          }
+          xs_smem[(m * p.xs_stride) / 8 + v] = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+      }
+    } else
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
       const int m = i / vec_per_row, v = i - m * vec_per_row;
       const int k = k_lo + 8 * v;
@@ -593,6 +632,15 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   }
   if (!store) return;
 
+  if (p.x_scale != nullptr) {  // FP8 activations: the per-token scale, before the bias
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int m = min(2 * L.c + (r & 1), p.M - 1);
+        v[t][r] *= __ldg(p.x_scale + m * p.x_scale_stride);
+      }
+  }
   // Fragment value r of tile t: row 4q + 2t (r < 2) or 4q + 2t + 1 (r >= 2), token 2c + (r & 1).
   const int split = static_cast<int>(blockIdx.y) / p.cluster;
   const bool direct = static_cast<int>(gridDim.y) == p.cluster;
@@ -703,6 +751,9 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   GemvParams p;
   p.x = reinterpret_cast<const __half*>(a.x);
   p.ldx = a.ldx;
+  p.x8 = a.x8;
+  p.x_scale = a.x_scale;
+  p.x_scale_stride = static_cast<int>(a.x_scale_stride);
   p.qw = a.qw;
   p.scales = reinterpret_cast<const __half*>(a.scales);
   p.qzeros = a.qzeros;

@@ -217,6 +217,69 @@ def _w4a16_dequant_fake(qweight_t, scales, qzeros, group_size):  # type: ignore[
     return qweight_t.new_empty((qweight_t.shape[0], qweight_t.shape[1] * 8), dtype=torch.float16)
 
 
+@torch.library.custom_op("tokenforge::w4a16_linear_fp8", mutates_args=())
+def w4a16_linear_fp8(
+    xq: torch.Tensor,
+    x_scale: torch.Tensor,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    bias: torch.Tensor | None,
+    group_size: int,
+) -> torch.Tensor:
+    """W4A16 linear on FP8 activations, the consumer of ``rmsnorm_fp8_quant``'s output:
+    ``x = e4m3(xq) * x_scale`` with ``x_scale`` one fp32 per token (``[..., 1]``) or a single
+    static value. No reference counterpart (the reference produces e4m3 activations only)."""
+    k = xq.shape[-1]
+    n = qweight_t.shape[0]
+    out_shape = (*xq.shape[:-1], n)
+    if xq.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise TypeError(f"xq must be float8_e4m3fn (or its uint8 codes), got {xq.dtype}")
+    if x_scale.dtype != torch.float32:
+        raise TypeError(f"x_scale must be fp32, got {x_scale.dtype}")
+    x2 = xq.reshape(-1, k)
+    m = x2.shape[0]
+    if m == 0:
+        return torch.empty(out_shape, dtype=torch.float16, device=xq.device)
+    if x_scale.numel() not in (1, m):
+        raise ValueError(f"x_scale must hold one value per token ({m}) or a single value, "
+                         f"got {x_scale.numel()}")
+    _check_inputs(torch.empty((m, k), dtype=torch.float16, device="meta"), qweight_t, scales,
+                  qzeros, group_size)
+    for name, t in (("xq", xq), ("x_scale", x_scale), ("qweight_t", qweight_t),
+                    ("scales", scales), ("qzeros", qzeros)):
+        _require(t, name)
+    if bias is not None:
+        _require(bias, "bias")
+        if tuple(bias.shape) != (n,) or bias.dtype != torch.float16:
+            raise ValueError(f"bias must be fp16 [{n}]")
+        bias = bias.contiguous()
+    x2 = x2.view(torch.uint8)
+    if x2.stride(-1) != 1 or x2.data_ptr() % 8 or (m > 1 and x2.stride(0) % 8):
+        x2 = x2.contiguous()
+        if x2.data_ptr() % 8:
+            x2 = x2.clone()
+    sc = x_scale.reshape(-1).contiguous()
+    y = torch.empty((m, n), dtype=torch.float16, device=xq.device)
+    lib = _lib.lib()
+    wsb = int(lib.tf_w4a16_fp8_workspace_bytes(m, n, k, group_size))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=xq.device) if wsb else None
+    with torch.cuda.device(xq.device):
+        status = lib.tf_w4a16_linear_fp8(
+            x2.data_ptr(), sc.data_ptr(), 0 if sc.numel() == 1 else 1, m, k, x2.stride(0),
+            qweight_t.data_ptr(), scales.data_ptr(), qzeros.data_ptr(), _lib.ptr(bias), n,
+            group_size, y.data_ptr(), n, _lib.ptr(ws), wsb, _lib.stream_ptr(xq.device),
+        )  # fmt: skip
+    _lib.check("tf_w4a16_linear_fp8", status)
+    return y.reshape(out_shape)
+
+
+@w4a16_linear_fp8.register_fake
+def _w4a16_linear_fp8_fake(xq, x_scale, qweight_t, scales, qzeros, bias, group_size):  # type: ignore[no-untyped-def]
+    return torch.empty((*xq.shape[:-1], qweight_t.shape[0]), dtype=torch.float16,
+                       device=xq.device)
+
+
 def rmsnorm_fp8_quant_2d(
     x: torch.Tensor, weight: torch.Tensor, eps: float, scale: torch.Tensor | None = None
 ) -> tuple[torch.Tensor, torch.Tensor]:
