@@ -390,6 +390,62 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- block stack (config 4)
+
+
+def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], steps: int) -> dict:
+    """the Qwen2.5-7B-shaped quantized block stack on the sweep's 28 layers of
+    weights. Per layer: rmsnorm_fp8_quant of the fp16 residual -> W4A16 qkv on the e4m3
+    activations -> the v slice (512 channels) repeated 7x stands in for attention -> W4A16 o ->
+    residual add -> rmsnorm_fp8_quant -> W4A16 gate_up on e4m3 -> SiLU * up -> W4A16 down ->
+    residual add. One step = the 28 layers on M tokens, replayed as a CUDA graph; tokens/s =
+    M / step time."""
+    import tokenforge_b200.ops as ops
+
+    gen = torch.Generator(device=device).manual_seed(123)
+    gammas = [((1 + 0.1 * torch.randn((2, HIDDEN), generator=gen, device=device))
+               .to(torch.float16)) for _ in sweep.layers]
+    out: dict[str, object] = {
+        "metric": "Qwen2.5-7B quantized block stack tokens/s (config 4, 28 layers, TP=1)",
+        "unit": "tokens/s",
+        "per_m": {},
+    }
+    for m in ms:
+        h0 = torch.randn((m, HIDDEN), generator=gen, device=device).to(torch.float16)
+
+        def step() -> None:
+            h = h0
+            for row, gamma in zip(sweep.layers, gammas):
+                w = {name: wt for name, wt, _ in row}
+                q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma[0], 1e-6, None)
+                qkv = torch.ops.tokenforge.w4a16_linear_fp8(
+                    q, sc, w["qkv"].qweight_t, w["qkv"].scales, w["qkv"].qzeros, None, G)
+                v = qkv[:, 4096:].repeat(1, 7)
+                h = h + ops.w4a16_gemm(v, w["o"].qweight_t, w["o"].scales, w["o"].qzeros, G)
+                q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma[1], 1e-6, None)
+                gu = torch.ops.tokenforge.w4a16_linear_fp8(
+                    q, sc, w["gate_up"].qweight_t, w["gate_up"].scales, w["gate_up"].qzeros,
+                    None, G)
+                a = ops.silu_mul(gu)
+                h = h + ops.w4a16_gemm(a, w["down"].qweight_t, w["down"].scales,
+                                       w["down"].qzeros, G)
+            step.out = h  # type: ignore[attr-defined]
+
+        g = capture(step, device)
+        g.replay()
+        torch.cuda.synchronize(device)
+        reps = max(2, steps if m <= 64 else steps // 4)
+        ms_step = time_graph(g, reps, device) / reps
+        finite = bool(torch.isfinite(step.out).all())  # type: ignore[attr-defined]
+        out["per_m"][str(m)] = {  # type: ignore[index]
+            "tokens_per_s": round(m / (ms_step * 1e-3), 1),
+            "ms_per_step": round(ms_step, 4),
+            "output_finite": finite,
+        }
+        del g
+    return out
+
+
 # ----------------------------------------------------------------------------- GEMM (config 2)
 
 
@@ -456,6 +512,7 @@ def main() -> None:
                     help="N > 1: all-reduce o/down with NCCL instead of inside the GEMV")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
+    ap.add_argument("--skip-block", action="store_true", help="omit the config-4 block-stack leg")
     ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
                     help="restrict the sweep to these layer types (profiling a small case)")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -583,6 +640,9 @@ def main() -> None:
     gemm = None
     if world == 1 and not args.skip_gemm:
         gemm = gemm_metric(device, args.gemm_m, max(3, args.steps // 2), 3, pk, src)
+    block = None
+    if world == 1 and full and not args.skip_block:
+        block = block_metric(sweep, device, (1, 64, 2048), max(3, args.steps // 2))
     cpu = None
     if rank == 0 and world == 1 and full and not args.skip_cpu:
         cpu = cpu_baseline(args.m, min_seconds=10.0)
@@ -630,6 +690,7 @@ def main() -> None:
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "gemm": gemm,
+            "block": block,
         }
         print(json.dumps(line), flush=True)
     del graph

@@ -173,6 +173,13 @@ TF_API int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t 
                     int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* SiLU-gated product of a fused gate_up projection (BASELINE config 4's block stack; no
+ * reference counterpart): out[m, i] = fp16(silu(g) * u), g = gate_up[m, i],
+ * u = gate_up[m, I + i], silu(g) = g / (1 + exp(-g)) in fp32. gate_up fp16 [M, 2I] with row
+ * stride ld, out fp16 [M, I] with row stride ldo. */
+TF_API int tf_silu_mul(const uint16_t* gate_up, int64_t M, int64_t I, int64_t ld, uint16_t* out,
+                       int64_t ldo, void* stream);
+
 /* ------------------------------------------------------- row-parallel all-reduce over NVLink
  * Tensor-parallel o / down layers (row-split K) end in a sum of every rank's fp16 partial
  * (NCCL all-reduce after o and down). tf_w4a16_linear_allreduce fuses that

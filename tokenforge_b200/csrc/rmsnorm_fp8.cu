@@ -204,6 +204,40 @@ __global__ void fp8_to_fp16_kernel(const uint8_t* __restrict__ q, int64_t M, int
   }
 }
 
+// out[m, i] = fp16(silu(g) * u) with g = gu[m, i], u = gu[m, I + i] (the fused gate_up
+// projection's two halves), silu(g) = g / (1 + e^-g) in fp32. Eight outputs per thread.
+__global__ void silu_mul_kernel(const __half* __restrict__ gu, int64_t M, int64_t I, int64_t ld,
+                                __half* __restrict__ out, int64_t ldo) {
+  const int64_t per_row = (I + 7) / 8;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= M * per_row) return;
+  const int64_t m = t / per_row, i0 = (t - m * per_row) * 8;
+  const __half* g = gu + m * ld + i0;
+  const __half* u = g + I;
+  __half* o = out + m * ldo + i0;
+  const bool vec = i0 + 8 <= I && ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u) |
+                                     reinterpret_cast<uintptr_t>(o)) & 15u) == 0;
+  if (vec) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(g), uv = *reinterpret_cast<const uint4*>(u);
+    const __half2* g2 = reinterpret_cast<const __half2*>(&gv);
+    const __half2* u2 = reinterpret_cast<const __half2*>(&uv);
+    uint4 ov;
+    __half2* o2 = reinterpret_cast<__half2*>(&ov);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 gf = __half22float2(g2[e]), uf = __half22float2(u2[e]);
+      o2[e] = __floats2half2_rn(gf.x / (1.0f + expf(-gf.x)) * uf.x,
+                                gf.y / (1.0f + expf(-gf.y)) * uf.y);
+    }
+    *reinterpret_cast<uint4*>(o) = ov;
+  } else {
+    for (int e = 0; e < 8 && i0 + e < I; ++e) {
+      const float gf = __half2float(g[e]), uf = __half2float(u[e]);
+      o[e] = __float2half_rn(gf / (1.0f + expf(-gf)) * uf);
+    }
+  }
+}
+
 }  // namespace
 
 int launch_fp8_to_fp16(const uint8_t* xq, int64_t M, int64_t K, int64_t ldq, const float* scale,
@@ -255,5 +289,18 @@ extern "C" int tf_cast_e4m3(const float* in, int64_t n, uint8_t* out, void* stre
   if (!in || !out) return TF_ERR_INVALID_ARG;
   cast_e4m3_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0,
                      static_cast<cudaStream_t>(stream)>>>(in, n, out);
+  return check_launch();
+}
+
+extern "C" int tf_silu_mul(const uint16_t* gate_up, int64_t M, int64_t I, int64_t ld, uint16_t* out,
+                           int64_t ldo, void* stream) {
+  using namespace tfb;
+  if (M < 0 || I < 1 || ld < 2 * I || ldo < I) return TF_ERR_INVALID_ARG;
+  if (M == 0) return TF_OK;
+  if (!gate_up || !out) return TF_ERR_INVALID_ARG;
+  const int64_t n = M * ((I + 7) / 8);
+  silu_mul_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0,
+                    static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __half*>(gate_up), M, I, ld, reinterpret_cast<__half*>(out), ldo);
   return check_launch();
 }

@@ -280,6 +280,25 @@ def _w4a16_linear_fp8_fake(xq, x_scale, qweight_t, scales, qzeros, bias, group_s
                        device=xq.device)
 
 
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """``gate_up [..., 2I] fp16 -> silu(gate) * up [..., I] fp16`` (fp32 inside, one rounding)."""
+    if gate_up.dtype != torch.float16:
+        raise TypeError(f"gate_up must be fp16, got {gate_up.dtype}")
+    if gate_up.shape[-1] % 2:
+        raise ValueError("gate_up's last dimension must be even (gate and up halves)")
+    _require(gate_up, "gate_up")
+    i = gate_up.shape[-1] // 2
+    g2 = gate_up.reshape(-1, 2 * i)
+    if g2.stride(-1) != 1:
+        g2 = g2.contiguous()
+    out = torch.empty((g2.shape[0], i), dtype=torch.float16, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        status = _lib.lib().tf_silu_mul(g2.data_ptr(), g2.shape[0], i, g2.stride(0),
+                                        out.data_ptr(), i, _lib.stream_ptr(gate_up.device))
+    _lib.check("tf_silu_mul", status)
+    return out.reshape(*gate_up.shape[:-1], i)
+
+
 def rmsnorm_fp8_quant_2d(
     x: torch.Tensor, weight: torch.Tensor, eps: float, scale: torch.Tensor | None = None
 ) -> tuple[torch.Tensor, torch.Tensor]:
