@@ -37,5 +37,5 @@ def test_silu_mul_strided_rows_and_extremes(device: torch.device) -> None:
     ref = _ref(base[:, :32])
     assert bool(torch.isfinite(y[:, :6]).all()) and bool(torch.isinf(y[:, 6]).all())
     ulp = torch.finfo(torch.float16).eps * ref.abs().clamp_min(2.0**-14)
-    assert bool(((y.double() - ref).abs() <= ulp)[:, :6].all())
-    assert bool((y[:, 7] == (_ref(base[:, :32])[:, 7]).half()).all())
+    ok = (y.double() - ref).abs() <= ulp
+    assert bool(ok[:, :6].all()) and bool(ok[:, 7:16].all())
