@@ -449,51 +449,125 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
 # ----------------------------------------------------------------------------- GEMM (config 2)
 
 
-def gemm_metric(device: torch.device, m: int, steps: int, warmup: int, pk: dict, src: str) -> dict:
+def gemm_metric(device: torch.device, ms: tuple[int, ...], steps: int, warmup: int, pk: dict,
+                src: str, headline_m: int = 1024) -> dict:
+    """gate_up + down W4A16 GEMM at each M, one CUDA graph per M."""
     from tokenforge_b200 import _lib
     from tokenforge_b200.config import launch_plan
 
     lib = _lib.lib()
     gen = torch.Generator(device=device).manual_seed(3)
-    calls, flops, names = [], 0, []
-    keep = []
+    layers = []
     for name, n, k, _ in (LAYER_SHAPES[2], LAYER_SHAPES[3]):
         qweight = torch.randint(-(2**31), 2**31 - 1, (k, n // 8), generator=gen, dtype=torch.int32, device=device)
         qz = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32, device=device)
         s = (torch.rand((k // G, n), generator=gen, device=device) * 0.018 + 0.002).to(torch.float16)
-        qt = torch.ops.tokenforge.awq_repack(qweight)
-        x = torch.randn((m, k), generator=gen, device=device).to(torch.float16)
-        y = torch.empty((m, n), dtype=torch.float16, device=device)
-        ws_b = int(lib.tf_w4a16_workspace_bytes(m, n, k, G))
-        ws = torch.empty(max(ws_b, 16), dtype=torch.uint8, device=device)
-        keep += [qt, qz, s, x, y, ws]
-        calls.append((x.data_ptr(), m, k, k, qt.data_ptr(), s.data_ptr(), qz.data_ptr(), None, n, G,
-                      y.data_ptr(), n, ws.data_ptr(), ws_b))
-        flops += 2 * m * n * k
-        names.append(f"{name} {launch_plan(m, n, k, G).kernel}")
+        layers.append((name, n, k, torch.ops.tokenforge.awq_repack(qweight), qz, s))
+        del qweight
+    per_m = {}
+    for m in ms:
+        calls, flops, names, keep = [], 0, [], []
+        for name, n, k, qt, qz, s in layers:
+            x = torch.randn((m, k), generator=gen, device=device).to(torch.float16)
+            y = torch.empty((m, n), dtype=torch.float16, device=device)
+            ws_b = int(lib.tf_w4a16_workspace_bytes(m, n, k, G))
+            ws = torch.empty(max(ws_b, 16), dtype=torch.uint8, device=device)
+            keep += [x, y, ws]
+            calls.append((x.data_ptr(), m, k, k, qt.data_ptr(), s.data_ptr(), qz.data_ptr(), None,
+                          n, G, y.data_ptr(), n, ws.data_ptr(), ws_b))
+            flops += 2 * m * n * k
+            names.append(f"{name} {launch_plan(m, n, k, G).kernel}")
+
+        def step() -> None:
+            st = torch.cuda.current_stream(device).cuda_stream
+            for a in calls:
+                rc = lib.tf_w4a16_linear(*a, st)
+                if rc != 0:
+                    raise RuntimeError(f"gemm failed: {rc}")
+
+        g = capture(step, device)
+        for _ in range(warmup):
+            g.replay()
+        reps = steps if m <= 1024 else max(3, steps // 4)
+        t_ms = time_graph(g, reps, device) / reps
+        del g
+        tflops = flops / (t_ms * 1e-3) / 1e12
+        per_m[str(m)] = {"tflops": round(tflops, 2), "ms_per_step": round(t_ms, 4),
+                         "frac": round(tflops / pk["bf16_tflops"], 4), "kernels": names}
+    head = per_m[str(headline_m)]
+    return {
+        "metric": f"W4A16 GEMM TFLOP/s at M={headline_m} (Qwen2.5-7B gate_up + down, config 2)",
+        "value": head["tflops"],
+        "unit": "TFLOP/s",
+        "ms_per_step": head["ms_per_step"],
+        "kernels": head["kernels"],
+        "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": head["frac"],
+                     "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
+        "per_m": per_m,
+        "l2": "weights 105 MB, x and y re-used across replays (tensor-bound above M ~ 256)",
+    }
+
+
+def repack_metric(device: torch.device, steps: int, pk: dict) -> dict:
+    """BASELINE config 2's load-time step: AWQ repack of gate_up and down (int32 read + write),
+    two copies of each alternated so that consecutive launches do not hit L2."""
+    gen = torch.Generator(device=device).manual_seed(4)
+    jobs, nbytes = [], 0
+    for _, n, k, _ in (LAYER_SHAPES[2], LAYER_SHAPES[3]):
+        for _ in range(2):
+            jobs.append(torch.randint(-(2**31), 2**31 - 1, (k, n // 8), generator=gen,
+                                      dtype=torch.int32, device=device))
+        nbytes += 2 * k * (n // 8) * 4  # read + write of one layer
+    outs: list[torch.Tensor] = []
 
     def step() -> None:
-        st = torch.cuda.current_stream(device).cuda_stream
-        for a in calls:
-            rc = lib.tf_w4a16_linear(*a, st)
-            if rc != 0:
-                raise RuntimeError(f"gemm failed: {rc}")
+        outs.clear()
+        for q in jobs[0::2]:
+            outs.append(torch.ops.tokenforge.awq_repack(q))
+        for q in jobs[1::2]:
+            outs.append(torch.ops.tokenforge.awq_repack(q))
 
     g = capture(step, device)
-    for _ in range(warmup):
+    g.replay()
+    t_ms = time_graph(g, steps, device) / steps / 2  # each step repacks every layer twice
+    gbs = nbytes / (t_ms * 1e-3) / 1e9
+    return {"metric": "AWQ repack GB/s (gate_up + down, read + write, config 2)",
+            "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(t_ms, 4),
+            "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4)}
+
+
+def rmsnorm_metric(device: torch.device, steps: int, pk: dict) -> dict:
+    """BASELINE config 1: fused RMSNorm + per-token e4m3 quant, H = 3584, T in {1, 256, 4096};
+    inputs fp16 ~N(0, 1) with 8 outlier channels x20, gamma ~N(1, 0.1). Enough input copies are
+    rotated that the bytes touched per replay exceed L2 for T = 4096."""
+    gen = torch.Generator(device=device).manual_seed(6)
+    out: dict[str, object] = {"metric": "RMSNorm + FP8 e4m3 quant GB/s (config 1, H = 3584)",
+                              "unit": "GB/s", "per_t": {}}
+    hidden = HIDDEN
+    outliers = torch.randperm(hidden, generator=torch.Generator().manual_seed(6))[:8]
+    gamma = (1 + 0.1 * torch.randn(hidden, generator=gen, device=device)).to(torch.float16)
+    for t in (1, 256, 4096):
+        per_call = t * hidden * 2 + hidden * 2 + t * hidden + t * 4
+        copies = max(2, min(64, -(-(256 << 20) // per_call)))
+        xs = []
+        for _ in range(copies):
+            x = torch.randn((t, hidden), generator=gen, device=device)
+            x[:, outliers.to(device)] *= 20
+            xs.append(x.to(torch.float16))
+
+        def step() -> None:
+            for x in xs:
+                torch.ops.tokenforge.rmsnorm_fp8_quant(x, gamma, 1e-6, None)
+
+        g = capture(step, device)
         g.replay()
-    ms = time_graph(g, steps, device) / steps
-    tflops = flops / (ms * 1e-3) / 1e12
-    return {
-        "metric": f"W4A16 GEMM TFLOP/s at M={m} (Qwen2.5-7B gate_up + down, config 2)",
-        "value": round(tflops, 2),
-        "unit": "TFLOP/s",
-        "ms_per_step": round(ms, 4),
-        "kernels": names,
-        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops"], 4),
-                     "peak_source": f"{src} bf16_tflops (burst)", "traffic": None},
-    }
+        t_ms = time_graph(g, max(3, steps // 2), device) / max(3, steps // 2) / copies
+        out["per_t"][str(t)] = {  # type: ignore[index]
+            "gbs": round(per_call / (t_ms * 1e-3) / 1e9, 1), "us_per_call": round(t_ms * 1e3, 3),
+            "frac_of_hbm": round(per_call / (t_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+        del g, xs
+    return out
 
 
 # ----------------------------------------------------------------------------- main
@@ -639,7 +713,12 @@ def main() -> None:
 
     gemm = None
     if world == 1 and not args.skip_gemm:
-        gemm = gemm_metric(device, args.gemm_m, max(3, args.steps // 2), 3, pk, src)
+        gemm = gemm_metric(device, tuple(sorted({16, 64, 256, 1024, 4096, args.gemm_m})),
+                           max(3, args.steps // 2), 3, pk, src, headline_m=args.gemm_m)
+    extra = {}
+    if world == 1 and full and not args.skip_gemm:
+        extra["repack"] = repack_metric(device, max(3, args.steps // 2), pk)
+        extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None
     if world == 1 and full and not args.skip_block:
         block = block_metric(sweep, device, (1, 64, 2048), max(3, args.steps // 2))
@@ -691,6 +770,7 @@ def main() -> None:
             "cpu_baseline": cpu,
             "gemm": gemm,
             "block": block,
+            **extra,
         }
         print(json.dumps(line), flush=True)
     del graph
