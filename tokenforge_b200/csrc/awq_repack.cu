@@ -90,6 +90,57 @@ __global__ void __launch_bounds__(128) awq_repack_kernel(const uint32_t* __restr
   }
 }
 
+// Tiled variant: a CTA of 128 threads turns 256 input rows x 32 input words into 256 output
+// rows x 32 output words (128 contiguous bytes each), staged through shared memory so that both
+// the loads (a warp reads 128 bytes of one input row) and the stores (eight threads write one
+// 128-byte output row segment) are full lines. Thread (cx, ky) transposes the 8 x 8 nibble
+// blocks of column word cx and row words 8ky .. 8ky+7 in registers as above.
+constexpr int kTileW = 32;             // input words per tile row = output words per tile row
+constexpr int kTileRows = 8 * kTileW;  // input rows per tile = output rows per tile
+__global__ void __launch_bounds__(128) awq_repack_tiled_kernel(const uint32_t* __restrict__ in,
+                                                               int64_t rows, int64_t cols8,
+                                                               uint32_t* __restrict__ out) {
+  __shared__ uint32_t tile[kTileRows][kTileW + 1];
+  const int cx = threadIdx.x & 31, ky = threadIdx.x >> 5;  // column word, row-word group
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * kTileW + cx;
+  const int64_t out_words = rows / 8;
+  const int64_t kw_base = static_cast<int64_t>(blockIdx.y) * kTileW;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const int wl = 8 * ky + b;  // output word within the tile
+    const int64_t kw = kw_base + wl;
+    uint32_t w[8];
+    if (c < cols8 && kw < out_words) {
+      const int64_t k0 = kw * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = __ldg(in + (k0 + kAwqOrder[j]) * cols8 + c);
+      transpose8x8_nibbles(w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = 0;
+    }
+    // Output row 8cx + s is kept at tile row 32s + cx: with a 33-word pitch the 32 threads of a
+    // warp (cx = 0..31) then write 32 different banks.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tile[32 * kAwqOrder[i] + cx][wl] = w[i];
+  }
+  __syncthreads();
+  // 256 output rows x 32 words: thread t writes 4 words of row (pass * 16 + t / 8).
+  const int sub = threadIdx.x & 7, rsub = threadIdx.x >> 3;
+  for (int r = rsub; r < kTileRows; r += 16) {
+    const int64_t orow = static_cast<int64_t>(blockIdx.x) * kTileRows + r;  // = 8 * c + s
+    if (orow >= cols8 * 8) break;
+    const int64_t kw = kw_base + 4 * sub;
+    uint32_t* dst = out + orow * out_words + kw;
+    const uint32_t* srow = &tile[32 * (r & 7) + (r >> 3)][4 * sub];
+    if (kw + 4 <= out_words && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(srow[0], srow[1], srow[2], srow[3]);
+    } else {
+      for (int e = 0; e < 4 && kw + e < out_words; ++e) dst[e] = srow[e];
+    }
+  }
+}
+
 int launch_repack(const int32_t* in, int64_t rows, int64_t cols, int32_t* out,
                   cudaStream_t stream) {
   // rows: the packed-across dimension of the output (K for repack); cols: logical columns.
@@ -98,6 +149,15 @@ int launch_repack(const int32_t* in, int64_t rows, int64_t cols, int32_t* out,
   if (in == nullptr || out == nullptr) return TF_ERR_INVALID_ARG;
   const int64_t cols8 = cols / 8;
   const int64_t out_words = rows / 8;
+  if (out_words >= kTileW && cols8 >= kTileW) {
+    const dim3 tgrid(static_cast<unsigned>(cdiv(cols8, kTileW)),
+                     static_cast<unsigned>(cdiv(out_words, kTileW)));
+    if (tgrid.y <= 65535u) {
+      awq_repack_tiled_kernel<<<tgrid, 128, 0, stream>>>(
+          reinterpret_cast<const uint32_t*>(in), rows, cols8, reinterpret_cast<uint32_t*>(out));
+      return check_launch();
+    }
+  }
   const dim3 block(128);
   const dim3 grid(static_cast<unsigned>(cdiv(cols8, 128)), static_cast<unsigned>(cdiv(out_words, 8)));
   if (grid.y > 65535u) return TF_ERR_UNSUPPORTED;

@@ -11,10 +11,10 @@
 // finite and infinite values to +-448, keeps NaN, and rounds to nearest even including the
 // subnormal range and the sign of zero (so -0.0 becomes code 0x80).
 //
-// Fast path: one warp per row with the row held in registers as fp16 (x is read from HBM once,
-// q written once): H/8 16-byte vectors spread over the 32 lanes, warp-shuffle reductions, no
-// shared memory. Generic path (any H, any alignment, H > 4096): one CTA per row, three sweeps
-// over the row (the second and third hit L2).
+// Fast paths hold the row in registers as fp16 (x is read from HBM once, q written once): one
+// warp per row for H <= 1024 (warp-shuffle reductions), one CTA per row up to H = 8192 (warp
+// shuffles + a shared-memory step). Generic path (any H, any alignment): one CTA per row, three
+// sweeps over the row (the second and third hit L2).
 #include "tf_common.cuh"
 #include "tf_plan.h"
 
@@ -103,6 +103,94 @@ __global__ void __launch_bounds__(128) rmsnorm_fp8_warp_kernel(
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int64_t j = lane + 32 * i;
+    if (j >= nvec) continue;
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+    uint32_t packed[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float2 a = __half22float2(h[2 * e]);
+      const float2 b = __half22float2(h[2 * e + 1]);
+      const uint32_t lo = cvt_e4m3x2(__fdiv_rn(a.x, scale), __fdiv_rn(a.y, scale));
+      const uint32_t hi = cvt_e4m3x2(__fdiv_rn(b.x, scale), __fdiv_rn(b.y, scale));
+      packed[e] = lo | (hi << 16);
+    }
+    qr[j] = make_uint2(packed[0], packed[1]);
+  }
+}
+
+// One CTA of NT threads per row (rows of H <= NT * VPT * 8, H % 8 == 0, aligned): each thread
+// holds VPT 16-byte vectors of the row in registers, so x is read once and q written once,
+// and a row's latency is that of two block reductions instead of a whole row per warp.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) rmsnorm_fp8_cta_kernel(
+    const uint4* __restrict__ x, int64_t T, int64_t H, int64_t ldx_vec,
+    const uint4* __restrict__ weight, float eps, const float* __restrict__ static_scale,
+    uint2* __restrict__ q, float* __restrict__ scale_out) {
+  __shared__ double sh_sum[NT / 32];
+  __shared__ float sh_max[NT / 32];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t nvec = H / 8;
+  const uint4* xr = x + row * ldx_vec;
+  uint4 v[VPT];
+  double sumsq = 0.0;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t j = tid + static_cast<int64_t>(NT) * i;
+    v[i] = (j < nvec) ? ldg_stream_v4(xr + j) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      sumsq += static_cast<double>(__fmul_rn(f.x, f.x)) + static_cast<double>(__fmul_rn(f.y, f.y));
+    }
+  }
+  sumsq = warp_sum(sumsq);
+  if (lane == 0) sh_sum[warp] = sumsq;
+  __syncthreads();
+  double total = 0.0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) total += sh_sum[w];
+  const float rstd = rstd_of(total, H, eps);
+
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t j = tid + static_cast<int64_t>(NT) * i;
+    if (j >= nvec) continue;
+    const uint4 wv = __ldg(weight + j);
+    __half2* h = reinterpret_cast<__half2*>(&v[i]);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      const __half2 n2 = __halves2half2(__float2half_rn(__fmul_rn(f.x, rstd)),
+                                        __float2half_rn(__fmul_rn(f.y, rstd)));
+      h[e] = __hmul2(n2, w2[e]);
+      const float2 y = __half22float2(h[e]);
+      amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
+    }
+  }
+  float scale;
+  if (static_scale != nullptr) {
+    scale = __ldg(static_scale);
+  } else {
+    amax = warp_max(amax);
+    if (lane == 0) sh_max[warp] = amax;
+    __syncthreads();
+    float m = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) m = fmaxf(m, sh_max[w]);
+    scale = dyn_scale(m);
+    if (tid == 0) scale_out[row] = scale;
+  }
+  uint2* qr = q + row * nvec;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t j = tid + static_cast<int64_t>(NT) * i;
     if (j >= nvec) continue;
     const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
     uint32_t packed[2];
@@ -267,12 +355,16 @@ extern "C" int tf_rmsnorm_fp8_quant(const uint16_t* x, int64_t T, int64_t H, int
   auto xv = reinterpret_cast<const uint4*>(x);
   auto wv = reinterpret_cast<const uint4*>(weight);
   auto qv = reinterpret_cast<uint2*>(q);
+  // Rows up to 1024 elements: a warp per row (four rows per CTA). Longer rows: a CTA per row
+  // (128 threads up to 4096 elements, 256 up to 8192), so that each row is short work.
   if (vec_ok && nvec <= 32 * 4) {
     rmsnorm_fp8_warp_kernel<4><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
-  } else if (vec_ok && nvec <= 32 * 8) {
-    rmsnorm_fp8_warp_kernel<8><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
-  } else if (vec_ok && nvec <= 32 * 16) {
-    rmsnorm_fp8_warp_kernel<16><<<grid, 128, 0, stream>>>(xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
+  } else if (vec_ok && nvec <= 128 * 4 && T <= 0x7fffffffLL) {
+    rmsnorm_fp8_cta_kernel<128, 4><<<static_cast<unsigned>(T), 128, 0, stream>>>(
+        xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
+  } else if (vec_ok && nvec <= 256 * 4 && T <= 0x7fffffffLL) {
+    rmsnorm_fp8_cta_kernel<256, 4><<<static_cast<unsigned>(T), 256, 0, stream>>>(
+        xv, T, H, ldx / 8, wv, eps, static_scale, qv, scale_out);
   } else {
     if (T > 0x7fffffffLL) return TF_ERR_UNSUPPORTED;
     rmsnorm_fp8_generic_kernel<<<static_cast<unsigned>(T), 256, 0, stream>>>(
