@@ -40,9 +40,18 @@ __device__ int g_device_error = 0;
 namespace {
 
 constexpr int kBlockN = 128;  // weight rows per tile = MMA M
-constexpr int kBlockK = 64;   // K per stage: one 128-byte swizzle row of fp16
-constexpr int kThreads = 384;
+constexpr int kBlockK = 64;   // K per swizzle atom: one 128-byte row of fp16
+// K per pipeline stage: two atoms (128) for token tiles of up to 64, where the per-stage
+// hand-offs, not the tensor core or HBM, set the pace; one atom for the larger tiles.
+__host__ __device__ constexpr int stage_k_for(int bm) { return bm <= 64 ? 128 : 64; }
 constexpr int kProducerWarp = 0, kMmaWarp = 1, kEpiWarp0 = 4, kDeqWarp0 = 8;
+// Dequant warps: 8 (two per SM sub-partition, each converting half of every row of a stage) for
+// the token tiles of up to 64, where the weight stream is the bottleneck and registers allow 16
+// warps; 4 for the tensor-bound larger tiles, whose epilogue needs more registers per thread.
+template <int BM>
+__host__ __device__ constexpr int deq_warps() { return BM <= 64 ? 8 : 4; }
+template <int BM>
+__host__ __device__ constexpr int cta_threads() { return 32 * (kDeqWarp0 + deq_warps<BM>()); }
 constexpr int kSmemLimit = 227 * 1024;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -56,24 +65,37 @@ enum WaitSite : int {
   kErrDrain = 0x107,
 };
 
-template <int BM>
+// Shared memory: a deep ring of packed stages (what TMA brings from HBM: x tile, int4 weight
+// tile, scale and zero-point rows) and a shallow ring of dequantized fp16 weight tiles. The
+// packed stages are small (about 7 KB at BM = 16), so many of them keep HBM busy while the
+// dequant warps and the tensor core work a few stages behind.
+template <int BM, int KB>
 struct TcLayout {
-  static constexpr int kXBytes = BM * 128;         // [BM x 64] fp16
-  static constexpr int kABytes = kBlockN * 128;    // [128 x 64] fp16
-  static constexpr int kWBytes = kBlockN * 32;     // [128 x 8] int32
-  static constexpr int kSBytes = 2 * kBlockN * 2;  // up to two group rows of 128 fp16
-  static constexpr int kZBytes = 2 * 16 * 4;       // up to two group rows of 16 int32
-  static constexpr int kAOff = kXBytes;
-  static constexpr int kWOff = kAOff + kABytes;
+  static constexpr int kAtoms = KB / kBlockK;       // 64-wide swizzle atoms per stage
+  static constexpr int kXAtom = BM * 128;           // [BM x 64] fp16 (MMA B operand)
+  static constexpr int kAAtom = kBlockN * 128;      // [128 x 64] fp16 (MMA A operand)
+  static constexpr int kXBytes = kAtoms * kXAtom;
+  static constexpr int kABytes = kAtoms * kAAtom;
+  static constexpr int kWBytes = kBlockN * KB / 2;  // [128 x KB/8] int32
+  static constexpr int kMaxGroups = KB / 32;        // group rows per stage at G = 32
+  static constexpr int kSBytes = kMaxGroups * kBlockN * 2;
+  static constexpr int kZBytes = kMaxGroups * 16 * 4;
+  static constexpr int kXOff = 0;                  // within a packed stage
+  static constexpr int kWOff = kXOff + kXBytes;
   static constexpr int kSOff = kWOff + kWBytes;
   static constexpr int kZOff = kSOff + kSBytes;
-  static constexpr int kStageBytes = ((kZOff + kZBytes) + 1023) / 1024 * 1024;
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kStagesFit = (kSmemLimit - 1024 - kBarrierBytes) / kStageBytes;
-  static constexpr int kStages = kStagesFit < 6 ? kStagesFit : 6;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+  static constexpr int kPStageBytes = ((kZOff + kZBytes) + 1023) / 1024 * 1024;
+  static constexpr int kAStages = KB == 128 ? 3 : (BM <= 64 ? 4 : (BM <= 128 ? 3 : 2));
+  static constexpr int kBarrierBytes = 1024;
+  static constexpr int kPStagesFit =
+      (kSmemLimit - 1024 - kBarrierBytes - kAStages * kABytes) / kPStageBytes;
+  static constexpr int kPStages = kPStagesFit < 32 ? kPStagesFit : 32;
+  static constexpr int kAOff0 = kPStages * kPStageBytes;  // first dequantized stage
+  static constexpr int kBarOff = kAOff0 + kAStages * kABytes;
+  static constexpr int kSmemBytes = 1024 + kBarOff + kBarrierBytes;
   static constexpr int kTmemCols = (2 * BM < 32) ? 32 : 2 * BM;  // power of two for BM = 16..256
-  static_assert(kStages >= 2, "shared memory too small for two stages");
+  static_assert(kPStages >= 2, "shared memory too small for two packed stages");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
 
 struct TcParams {
@@ -268,30 +290,40 @@ __device__ __forceinline__ Unit decode_unit(int u, const TcParams& p) {
   return w;
 }
 
-template <int BM>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BM, int KB>
+__global__ void __launch_bounds__(cta_threads<BM>(), 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                     const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_s,
                     const __grid_constant__ CUtensorMap tm_z, const TcParams p) {
-  using L = TcLayout<BM>;
-  constexpr int S = L::kStages;
+  using L = TcLayout<BM, KB>;
+  constexpr int SP = L::kPStages, SA = L::kAStages;
+  constexpr int kDeq = deq_warps<BM>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * L::kStageBytes);
-  uint64_t* deq = full + S;
-  uint64_t* empty = deq + S;
-  uint64_t* acc_full = empty + S;
+  // pfull: the stage's TMA bytes landed. pempty: the dequant warps read its weights (one
+  // arrival each) and the MMAs that read its x tile completed (1). afull: the dequant warps
+  // wrote the fp16 tile. aempty: the MMAs that read it completed.
+  uint64_t* pfull = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* pempty = pfull + SP;
+  uint64_t* afull = pempty + SP;
+  uint64_t* aempty = afull + SA;
+  uint64_t* acc_full = aempty + SA;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  auto pstage = [&](uint32_t s) { return smem + s * L::kPStageBytes; };
+  auto astage = [&](uint32_t a) { return smem + L::kAOff0 + a * L::kABytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&deq[s], 4);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SP; ++s) {
+      mbar_init(&pfull[s], 1);
+      mbar_init(&pempty[s], kDeq + 1);
+    }
+    for (int a = 0; a < SA; ++a) {
+      mbar_init(&afull[a], kDeq);
+      mbar_init(&aempty[a], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -321,24 +353,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit w = decode_unit(u, p);
         const int m0 = w.m_tile * BM;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
-          const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, kErrProducerEmpty)) {
+          const uint32_t s = it % SP, ph = (it / SP) & 1u;
+          if (!mbar_wait(&pempty[s], ph ^ 1u, kErrProducerEmpty)) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * L::kStageBytes;
-          const int g0 = (kb * kBlockK) / p.group_size;
-          mbar_expect_tx(&full[s], p.tx_bytes);
-          tma_load_2d(st, &tm_x, &full[s], kb * kBlockK, m0);
-          tma_load_2d(st + L::kWOff, &tm_w, &full[s], kb * (kBlockK / 8), static_cast<int>(w.n0));
-          tma_load_2d(st + L::kSOff, &tm_s, &full[s], static_cast<int>(w.n0), g0);
-          tma_load_2d(st + L::kZOff, &tm_z, &full[s], static_cast<int>(w.n0 / 8), g0);
+          uint8_t* st = pstage(s);
+          const int g0 = (kb * KB) / p.group_size;
+          mbar_expect_tx(&pfull[s], p.tx_bytes);
+#pragma unroll
+          for (int at = 0; at < L::kAtoms; ++at)
+            tma_load_2d(st + L::kXOff + at * L::kXAtom, &tm_x, &pfull[s], kb * KB + at * kBlockK,
+                        m0);
+          tma_load_2d(st + L::kWOff, &tm_w, &pfull[s], kb * (KB / 8), static_cast<int>(w.n0));
+          tma_load_2d(st + L::kSOff, &tm_s, &pfull[s], static_cast<int>(w.n0), g0);
+          tma_load_2d(st + L::kZOff, &tm_z, &pfull[s], static_cast<int>(w.n0 / 8), g0);
         }
       }
       // Drain: every armed stage must have landed before the CTA may exit.
-      const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+      const uint32_t first = it > static_cast<uint32_t>(SP) ? it - SP : 0;
       for (uint32_t j = first; j < it; ++j)
-        if (!mbar_wait(&full[j % S], (j / S) & 1u, kErrDrain)) break;
+        if (!mbar_wait(&pfull[j % SP], (j / SP) & 1u, kErrDrain)) break;
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -346,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, tc = 0;
       bool ok = true;
       bool issued = false;
-      uint32_t last_s = 0, last_ph = 0;
+      uint32_t last_a = 0, last_aph = 0;
       for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++tc) {
         const Unit w = decode_unit(u, p);
         const uint32_t b = tc & 1u, aph = (tc >> 1) & 1u;
@@ -357,29 +392,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BM;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
-          const uint32_t s = it % S, ph = (it / S) & 1u;
-          if (!mbar_wait(&deq[s], ph, kErrMmaDeq) || !mbar_wait(&full[s], ph, kErrMmaFull)) {
+          const uint32_t s = it % SP, ph = (it / SP) & 1u;
+          const uint32_t a = it % SA, aph = (it / SA) & 1u;
+          if (!mbar_wait(&afull[a], aph, kErrMmaDeq) || !mbar_wait(&pfull[s], ph, kErrMmaFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint8_t* st = smem + s * L::kStageBytes;
-          const uint64_t a_desc = sw128_desc(smem_u32(st + L::kAOff));
-          const uint64_t b_desc = sw128_desc(smem_u32(st));
 #pragma unroll
-          for (int kk = 0; kk < kBlockK / 16; ++kk)
-            umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc,
-                     (kb > w.kb0 || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+          for (int at = 0; at < L::kAtoms; ++at) {
+            const uint64_t a_desc = sw128_desc(smem_u32(astage(a) + at * L::kAAtom));
+            const uint64_t b_desc = sw128_desc(smem_u32(pstage(s) + L::kXOff + at * L::kXAtom));
+#pragma unroll
+            for (int kk = 0; kk < kBlockK / 16; ++kk)
+              umma_f16(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc,
+                       (kb > w.kb0 || at > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&pempty[s]);
+          umma_commit(&aempty[a]);
           issued = true;
-          last_s = s;
-          last_ph = ph;
+          last_a = a;
+          last_aph = aph;
         }
         if (!ok) break;
         umma_commit(&acc_full[b]);
       }
       // Error exit: let the MMAs already issued finish before the TMEM is released.
-      if (!ok && issued) mbar_wait(&empty[last_s], last_ph, kErrDrain);
+      if (!ok && issued) mbar_wait(&aempty[last_a], last_aph, kErrDrain);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     const int q = warp - kEpiWarp0;  // TMEM lanes 32q .. 32q+31
@@ -422,47 +461,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
-  } else if (warp >= kDeqWarp0 && warp < kDeqWarp0 + 4) {
-    const int t = threadIdx.x - kDeqWarp0 * 32;  // weight row within the tile
-    const int two_groups = p.group_size < kBlockK;  // G = 32: two groups per K block
+  } else if (warp >= kDeqWarp0 && warp < kDeqWarp0 + kDeq) {
+    const int d = warp - kDeqWarp0;
+    const int t = 32 * (d & 3) + lane;             // weight row within the tile
+    constexpr int kRowWords = KB / 8;              // packed words of a row per stage
+    constexpr int kWords = kRowWords / (kDeq / 4);  // of them, converted by this thread
+    const int j0 = (d >> 2) * kWords;              // first of them
+    const int gshift = p.group_size == 32 ? 2 : (p.group_size == 64 ? 3 : 4);  // word -> group
+    const int nib = 4 * awq_nibble_of(t & 7);
     uint32_t it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
       const Unit w = decode_unit(u, p);
       for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
-        const uint32_t s = it % S, ph = (it / S) & 1u;
-        if (!mbar_wait(&full[s], ph, kErrDeqFull)) {
+        const uint32_t s = it % SP, ph = (it / SP) & 1u;
+        const uint32_t a = it % SA, aph = (it / SA) & 1u;
+        if (!mbar_wait(&pfull[s], ph, kErrDeqFull) ||
+            !mbar_wait(&aempty[a], aph ^ 1u, kErrDeqFull)) {
           ok = false;
           break;
         }
-        uint8_t* st = smem + s * L::kStageBytes;
-        const uint4* wrow = reinterpret_cast<const uint4*>(st + L::kWOff + t * 32);
-        const uint4 w0 = wrow[0], w1 = wrow[1];
+        uint8_t* st = pstage(s);
+        const uint32_t* wrow = reinterpret_cast<const uint32_t*>(st + L::kWOff + t * (KB / 2)) + j0;
+        uint32_t words[kWords];
+#pragma unroll
+        for (int j = 0; j < kWords; j += 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(wrow + j);
+          words[j] = v.x;
+          words[j + 1] = v.y;
+          words[j + 2] = v.z;
+          words[j + 3] = v.w;
+        }
         const __half* srow = reinterpret_cast<const __half*>(st + L::kSOff);
         const uint32_t* zrow = reinterpret_cast<const uint32_t*>(st + L::kZOff);
-        const int nib = 4 * awq_nibble_of(t & 7);
-        const __half s0 = srow[t];
-        const __half s1 = two_groups ? srow[kBlockN + t] : s0;
-        const uint32_t z0 = (zrow[t >> 3] >> nib) & 0xFu;
-        const uint32_t z1 = two_groups ? ((zrow[16 + (t >> 3)] >> nib) & 0xFu) : z0;
-        const __half2 zz0 = zero_magic2(z0), zz1 = zero_magic2(z1);
-        const __half2 ss0 = __halves2half2(s0, s0), ss1 = __halves2half2(s1, s1);
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint8_t* arow = st + L::kAOff + t * 128;
+        // The stage's group rows start at its first group; word j of the row is in group
+        // (j >> gshift) of those (at most one group per stage when G >= KB).
+        uint8_t* arow = astage(a) + t * 128;
+        int gcur = -1;
+        __half2 zz, ss;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const __half2 zz = j < 4 ? zz0 : zz1;
-          const __half2 ss = j < 4 ? ss0 : ss1;
+        for (int jj = 0; jj < kWords; ++jj) {
+          const int j = j0 + jj;  // 16-byte chunk j of the row: k offsets 8j .. 8j+7
+          const int gi = p.group_size >= KB ? 0 : (j >> gshift);
+          if (gi != gcur) {
+            gcur = gi;
+            const __half sv = srow[gi * kBlockN + t];
+            const uint32_t zv = (zrow[gi * 16 + (t >> 3)] >> nib) & 0xFu;
+            zz = zero_magic2(zv);
+            ss = __halves2half2(sv, sv);
+          }
           uint4 o;
-          o.x = dequant_pair(magic_pair(words[j], 0), zz, ss);
-          o.y = dequant_pair(magic_pair(words[j], 1), zz, ss);
-          o.z = dequant_pair(magic_pair(words[j], 2), zz, ss);
-          o.w = dequant_pair(magic_pair(words[j], 3), zz, ss);
-          *reinterpret_cast<uint4*>(arow + ((j ^ (t & 7)) << 4)) = o;
+          o.x = dequant_pair(magic_pair(words[jj], 0), zz, ss);
+          o.y = dequant_pair(magic_pair(words[jj], 1), zz, ss);
+          o.z = dequant_pair(magic_pair(words[jj], 2), zz, ss);
+          o.w = dequant_pair(magic_pair(words[jj], 3), zz, ss);
+          const int at = j >> 3, ch = j & 7;
+          *reinterpret_cast<uint4*>(arow + at * L::kAAtom + ((ch ^ (t & 7)) << 4)) = o;
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&deq[s]);
+        if (lane == 0) {
+          mbar_arrive(&afull[a]);
+          mbar_arrive(&pempty[s]);
+        }
       }
     }
   }
@@ -511,15 +572,15 @@ int num_sms() {
   return n;
 }
 
-template <int BM>
+template <int BM, int KB>
 int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
-  using L = TcLayout<BM>;
+  using L = TcLayout<BM, KB>;
   const int G = a.group_size;
-  const uint32_t rows = G < kBlockK ? 2u : 1u;  // group rows per K block
+  const uint32_t rows = G < KB ? static_cast<uint32_t>(KB / G) : 1u;  // group rows per stage
   CUtensorMap mx, mw, ms, mz;
   if (!make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, a.K, a.M, a.ldx * 2, kBlockK, BM,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, a.qw, a.K / 8, a.N, a.K / 2, kBlockK / 8,
+      !make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, a.qw, a.K / 8, a.N, a.K / 2, KB / 8,
                 kBlockN, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.scales, a.N, a.K / G, a.N * 2, kBlockN,
                 rows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -534,10 +595,11 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
   p.group_size = G;
   p.m_tiles = static_cast<int>(cdiv(a.M, BM));
   p.k_splits = pl.split_k;
-  p.kb_total = static_cast<int>(a.K / kBlockK);
+  p.kb_total = static_cast<int>(a.K / KB);
   p.kb_per_split = pl.blocks_per_split;
   p.units = static_cast<int>(cdiv(a.N, kBlockN)) * p.m_tiles * p.k_splits;
   p.tx_bytes = static_cast<uint32_t>(L::kXBytes + L::kWBytes + rows * (kBlockN * 2) + rows * 64);
+  static_assert(L::kXBytes % 1024 == 0 && L::kWOff % 16 == 0, "stage layout alignment");
   p.bias = reinterpret_cast<const __half*>(a.bias);
   p.y = reinterpret_cast<__half*>(a.y);
   p.ldy = a.ldy;
@@ -548,8 +610,8 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(w4a16_tc_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    L::kSmemBytes);
+    attr_err = cudaFuncSetAttribute(w4a16_tc_kernel<BM, KB>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmemBytes);
   });
   if (attr_err != cudaSuccess) {
     last_cuda_error() = static_cast<int>(attr_err);
@@ -558,7 +620,7 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(std::min(p.units, num_sms())));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(cta_threads<BM>());
   cfg.dynamicSmemBytes = L::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -566,7 +628,7 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (launch_flags() & TF_LAUNCH_PDL) ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<BM>, mx, mw, ms, mz, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, w4a16_tc_kernel<BM, KB>, mx, mw, ms, mz, p);
   if (e != cudaSuccess) {
     last_cuda_error() = static_cast<int>(e);
     return TF_ERR_CUDA;
@@ -586,16 +648,23 @@ bool tc_gemm_supported(int64_t M, int64_t N, int64_t K, int group_size) {
 // Work split for the tensor-core GEMM: tile_m by bucket, then the number of K splits that
 // minimises the busiest CTA's share of K blocks over 148 persistent CTAs (at least 8 blocks per
 // split), preferring fewer splits on ties.
+int tc_stage_k(int tile_m, int64_t K) {
+  const int kb = stage_k_for(tile_m);
+  return K % kb == 0 ? kb : kBlockK;
+}
+
 void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   const int64_t n_tiles = cdiv(N, kBlockN), m_tiles = cdiv(M, pl->tile_m);
   const int64_t base = n_tiles * m_tiles;
-  const int64_t kb = K / kBlockK;
+  const int stage_k = tc_stage_k(pl->tile_m, K);
+  const int64_t kb = K / stage_k;
+  const int64_t min_per = 8 * kBlockK / stage_k;  // at least 512 of K per split
   const int sms = 148;
   int best_s = 1;
   double best = static_cast<double>(cdiv(base, sms));
   for (int s = 2; s <= 8; ++s) {
     const int64_t per = cdiv(kb, s);
-    if (per < 8) break;
+    if (per < min_per) break;
     const int64_t splits = cdiv(kb, per);
     const double t = static_cast<double>(cdiv(base * splits, sms)) * per / kb;
     if (t < best * 0.97) {
@@ -616,12 +685,13 @@ void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
 }
 
 int launch_tc_gemm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
+  const bool wide = tc_stage_k(pl.tile_m, a.K) == 128;
   switch (pl.tile_m) {
-    case 16: return launch_bm<16>(pl, a, stream);
-    case 32: return launch_bm<32>(pl, a, stream);
-    case 64: return launch_bm<64>(pl, a, stream);
-    case 128: return launch_bm<128>(pl, a, stream);
-    case 256: return launch_bm<256>(pl, a, stream);
+    case 16: return wide ? launch_bm<16, 128>(pl, a, stream) : launch_bm<16, 64>(pl, a, stream);
+    case 32: return wide ? launch_bm<32, 128>(pl, a, stream) : launch_bm<32, 64>(pl, a, stream);
+    case 64: return wide ? launch_bm<64, 128>(pl, a, stream) : launch_bm<64, 64>(pl, a, stream);
+    case 128: return launch_bm<128, 64>(pl, a, stream);
+    case 256: return launch_bm<256, 64>(pl, a, stream);
     default: return TF_ERR_UNSUPPORTED;
   }
 }
