@@ -580,7 +580,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--gemm-m", type=int, default=1024)
+    ap.add_argument("--gemm-m", type=int, default=1024, help="M of the GEMM headline")
+    ap.add_argument("--gemm-ms", type=str, default="16,64,256,1024,4096",
+                    help="comma-separated M values of the GEMM leg (config 2)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-fuse", action="store_true",
                     help="N > 1: all-reduce o/down with NCCL instead of inside the GEMV")
@@ -713,7 +715,8 @@ def main() -> None:
 
     gemm = None
     if world == 1 and not args.skip_gemm:
-        gemm = gemm_metric(device, tuple(sorted({16, 64, 256, 1024, 4096, args.gemm_m})),
+        gemm_ms = {int(v) for v in args.gemm_ms.split(",") if v} | {args.gemm_m}
+        gemm = gemm_metric(device, tuple(sorted(gemm_ms)),
                            max(3, args.steps // 2), 3, pk, src, headline_m=args.gemm_m)
     extra = {}
     if world == 1 and full and not args.skip_gemm:
