@@ -85,7 +85,9 @@ struct TcLayout {
   static constexpr int kSOff = kWOff + kWBytes;
   static constexpr int kZOff = kSOff + kSBytes;
   static constexpr int kPStageBytes = ((kZOff + kZBytes) + 1023) / 1024 * 1024;
-  static constexpr int kAStages = KB == 128 ? 3 : (BM <= 64 ? 4 : (BM <= 128 ? 3 : 2));
+  // Dequantized tiles in flight: the tensor-bound large tiles need four so that the dequant
+  // warps run ahead of the MMAs (two measured 20% slower at M = 1024).
+  static constexpr int kAStages = KB == 128 ? 3 : 4;
   static constexpr int kBarrierBytes = 1024;
   static constexpr int kPStagesFit =
       (kSmemLimit - 1024 - kBarrierBytes - kAStages * kABytes) / kPStageBytes;
@@ -495,21 +497,11 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
         const __half* srow = reinterpret_cast<const __half*>(st + L::kSOff);
         const uint32_t* zrow = reinterpret_cast<const uint32_t*>(st + L::kZOff);
         // The stage's group rows start at its first group; word j of the row is in group
-        // (j >> gshift) of those (at most one group per stage when G >= KB).
+        // (j >> gshift) of those. One group per stage (G >= KB, e.g. G = 128) takes the path
+        // with the zero point and scale held in registers for the whole row.
         uint8_t* arow = astage(a) + t * 128;
-        int gcur = -1;
-        __half2 zz, ss;
-#pragma unroll
-        for (int jj = 0; jj < kWords; ++jj) {
+        auto convert = [&](int jj, __half2 zz, __half2 ss) {
           const int j = j0 + jj;  // 16-byte chunk j of the row: k offsets 8j .. 8j+7
-          const int gi = p.group_size >= KB ? 0 : (j >> gshift);
-          if (gi != gcur) {
-            gcur = gi;
-            const __half sv = srow[gi * kBlockN + t];
-            const uint32_t zv = (zrow[gi * 16 + (t >> 3)] >> nib) & 0xFu;
-            zz = zero_magic2(zv);
-            ss = __halves2half2(sv, sv);
-          }
           uint4 o;
           o.x = dequant_pair(magic_pair(words[jj], 0), zz, ss);
           o.y = dequant_pair(magic_pair(words[jj], 1), zz, ss);
@@ -517,6 +509,21 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
           o.w = dequant_pair(magic_pair(words[jj], 3), zz, ss);
           const int at = j >> 3, ch = j & 7;
           *reinterpret_cast<uint4*>(arow + at * L::kAAtom + ((ch ^ (t & 7)) << 4)) = o;
+        };
+        if (p.group_size >= KB) {
+          const __half sv = srow[t];
+          const __half2 zz = zero_magic2((zrow[t >> 3] >> nib) & 0xFu);
+          const __half2 ss = __halves2half2(sv, sv);
+#pragma unroll
+          for (int jj = 0; jj < kWords; ++jj) convert(jj, zz, ss);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < kWords; ++jj) {
+            const int gi = (j0 + jj) >> gshift;
+            const __half sv = srow[gi * kBlockN + t];
+            convert(jj, zero_magic2((zrow[gi * 16 + (t >> 3)] >> nib) & 0xFu),
+                    __halves2half2(sv, sv));
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
