@@ -173,6 +173,24 @@ TF_API int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t 
                     int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Fused RMSNorm + FP8 quantization + W4A16 linear for decode (M <= 8): one kernel computes
+ *   (q, s) = rmsnorm_fp8_quant(x, norm_weight, eps, static_scale) and y = w4a16_linear_fp8(q, s),
+ * with y bit-identical to calling tf_rmsnorm_fp8_quant and then tf_w4a16_linear_fp8. Each CTA
+ * normalises and quantises the rows in its shared memory, so neither the codes nor the
+ * normalised activations go to HBM and one launch replaces two. No reference counterpart: it is
+ * the fused RMSNorm -> quant -> GEMV prologue that the reference's e4m3 output lacks a consumer
+ * for. x: fp16 [M, K] (16-byte aligned, ldx % 8 == 0); norm_weight: fp16 [K], 16-byte aligned;
+ * static_scale: one fp32 or NULL (dynamic per-token scales, written to scale_out [M] when it is
+ * not NULL). Returns TF_ERR_UNSUPPORTED (launching nothing) for M > 8 and for layers whose
+ * decode plan splits K across CTAs; the caller then makes the two calls. Workspace as
+ * tf_w4a16_linear (none for the plans it accepts). */
+TF_API int tf_rmsnorm_fp8_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                    const uint16_t* norm_weight, float eps, const float* static_scale,
+                    float* scale_out, const int32_t* qweight_t, const uint16_t* scales,
+                    const int32_t* qzeros, const uint16_t* bias, int64_t N, int32_t group_size,
+                    uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
 /* SiLU-gated product of a fused gate_up projection (BASELINE config 4's block stack; no
  * reference counterpart): out[m, i] = fp16(silu(g) * u), g = gate_up[m, i],
  * u = gate_up[m, I + i], silu(g) = g / (1 + exp(-g)) in fp32. gate_up fp16 [M, 2I] with row

@@ -231,6 +231,10 @@ LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const
   a.x8 = nullptr;
   a.x_scale = nullptr;
   a.x_scale_stride = 0;
+  a.norm_w = nullptr;
+  a.norm_eps = 0.f;
+  a.norm_static = nullptr;
+  a.norm_scale_out = nullptr;
   a.x = x;
   a.M = M;
   a.K = K;
@@ -512,6 +516,39 @@ int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t scale_s
                            static_cast<char*>(workspace) + x16_bytes,
                            workspace_bytes - x16_bytes);
   return run_linear(a, stream, -1);
+}
+
+int tf_rmsnorm_fp8_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
+                                const uint16_t* norm_weight, float eps,
+                                const float* static_scale, float* scale_out,
+                                const int32_t* qweight_t, const uint16_t* scales,
+                                const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                                int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  using namespace tfb;
+  if (M < 0 || K < 1) return TF_ERR_INVALID_ARG;
+  if (M == 0) return TF_OK;
+  if (!norm_weight) return TF_ERR_INVALID_ARG;
+  if (M > 8 || K % 8 != 0) return TF_ERR_UNSUPPORTED;
+  if (!aligned16(norm_weight)) return TF_ERR_ALIGNMENT;
+  auto a = make_args(x, M, K, ldx, qweight_t, scales, qzeros, bias, N, group_size, y, ldy,
+                     workspace, workspace_bytes);
+  a.norm_w = norm_weight;
+  a.norm_eps = eps;
+  a.norm_static = static_scale;
+  a.norm_scale_out = static_scale ? nullptr : scale_out;
+  int st = validate_linear(a);
+  if (st != TF_OK) return st;
+  LinearPlan pl;
+  st = plan_linear(M, N, K, group_size, &pl);
+  if (st != TF_OK) return st;
+  // One pass: every CTA must hold whole rows (no K split across CTAs).
+  if (pl.kernel != kKernelGemv || !gemv_fits(M, N, K, ldx, group_size) || pl.split_k != 1 ||
+      pl.cluster != 1)
+    return TF_ERR_UNSUPPORTED;
+  if (pl.workspace > 0 && (workspace == nullptr || workspace_bytes < pl.workspace))
+    return TF_ERR_WORKSPACE;
+  return launch_gemv(pl, a, static_cast<cudaStream_t>(stream));
 }
 
 int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,

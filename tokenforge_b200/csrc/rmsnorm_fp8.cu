@@ -17,35 +17,11 @@
 // sweeps over the row (the second and third hit L2).
 #include "tf_common.cuh"
 #include "tf_plan.h"
+#include "tf_rmsnorm.cuh"
 
 namespace tfb {
 namespace {
 
-constexpr float kFp8Max = 448.0f;
-constexpr float kMinScale = 1.0f / (448.0f * 512.0f);
-
-__device__ __forceinline__ double warp_sum(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// The sum of squares is accumulated in fp64: every fp16 square is exact in fp32 and the fp64 sum
-// of up to ~1e6 of them is exact or within 2^-53, so its fp32 rounding does not depend on the
-// summation order (threads, warps, the CPU oracle all obtain the same fp32 sum).
-__device__ __forceinline__ float rstd_of(double sumsq, int64_t H, float eps) {
-  const float var = __fdiv_rn(__double2float_rn(sumsq), static_cast<float>(H));
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-}
-
-__device__ __forceinline__ float dyn_scale(float amax) {
-  return fmaxf(__fdiv_rn(amax, kFp8Max), kMinScale);
-}
 
 // VPL = 16-byte vectors per lane; rows of H <= 256 * VPL elements, H % 8 == 0, aligned.
 template <int VPL>

@@ -53,6 +53,13 @@ struct LinearArgs {
   const uint8_t* x8;
   const float* x_scale;
   int64_t x_scale_stride;
+  // Fused RMSNorm + FP8 prologue of the decode GEMV (norm_w != null): x is normalised with
+  // norm_w and eps, quantised to e4m3 with the static scale (or per token, written to
+  // norm_scale_out when not null), and the GEMV consumes the codes.
+  const uint16_t* norm_w;
+  float norm_eps;
+  const float* norm_static;
+  float* norm_scale_out;
 };
 
 // One rank's mailbox: a 256-byte header (u32 call counter, arrival counter, error word), then

@@ -30,6 +30,7 @@
 // one cluster write fp32 partials that a second kernel reduces in split order.
 #include "tf_common.cuh"
 #include "tf_plan.h"
+#include "tf_rmsnorm.cuh"
 
 namespace tfb {
 namespace {
@@ -66,6 +67,12 @@ struct GemvParams {
   int peer_participants;                  // storing warps of the grid (one per 32-row tile)
   uint32_t* peer_ctl;                     // own mailbox header: call counter, arrivals, error
   uint64_t* peer_data[TF_MAX_PEERS];       // rank q's tagged partials [2][world][max_m][max_n]
+  // Fused RMSNorm + FP8 prologue (kernels instantiated with kNorm): x is the un-normalised fp16
+  // input, norm_w the RMSNorm weight [K]; every CTA covers the whole row.
+  const __half* norm_w;
+  float norm_eps;
+  const float* norm_static;  // static per-tensor scale, or null for the dynamic per-token one
+  float* norm_scale_out;     // per-token scales [M] (dynamic case; written by CTA 0), or null
 };
 
 // One K block of this lane's four rows, in registers from issue to use.
@@ -430,7 +437,93 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
-template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact>
+// Fused RMSNorm + FP8 prologue on the staged rows (the CTA holds all K of each of the M rows):
+// the rule of rmsnorm_fp8_quant (tf_rmsnorm.cuh) applied in shared memory. Pass 1 sums the
+// squares in fp64, pass 2 writes y = fp16(x * rstd) * weight in place and takes amax|y|, pass 3
+// replaces y by the exact fp16 value of its e4m3 code e4m3(y / scale). The GEMV then runs
+// exactly as on rmsnorm_fp8_quant's (codes, scale) and multiplies y by scale[m] in fp32, so its
+// output is bit-identical to the two-kernel path. red: >= 3 * 8 * warps floats of scratch.
+__device__ __noinline__ void norm_quant_staged(const GemvParams& p, uint4* xs, float* red,
+                                               float* scale_sh) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = static_cast<int>(blockDim.x) >> 5, nt = static_cast<int>(blockDim.x);
+  const int nvec = p.K / 8;
+  double* sh_sum = reinterpret_cast<double*>(red);  // [M][nw]
+  float* sh_max = red + 2 * 8 * nw;                 // [M][nw]
+  const uint4* wv = reinterpret_cast<const uint4*>(p.norm_w);
+  for (int m = 0; m < p.M; ++m) {
+    const uint4* row = xs + (m * p.xs_stride) / 8;
+    double s = 0.0;
+    for (int j = tid; j < nvec; j += nt) {
+      const uint4 v = row[j];
+      const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        s += static_cast<double>(__fmul_rn(f.x, f.x)) + static_cast<double>(__fmul_rn(f.y, f.y));
+      }
+    }
+    s = warp_sum(s);
+    if (lane == 0) sh_sum[m * nw + warp] = s;
+  }
+  __syncthreads();
+  for (int m = 0; m < p.M; ++m) {
+    double tot = 0.0;
+    for (int w = 0; w < nw; ++w) tot += sh_sum[m * nw + w];
+    const float rstd = rstd_of(tot, p.K, p.norm_eps);
+    uint4* row = xs + (m * p.xs_stride) / 8;
+    float amax = 0.f;
+    for (int j = tid; j < nvec; j += nt) {
+      uint4 v = row[j];
+      const uint4 g = __ldg(wv + j);
+      __half2* h = reinterpret_cast<__half2*>(&v);
+      const __half2* g2 = reinterpret_cast<const __half2*>(&g);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h[e]);
+        const __half2 n2 = __halves2half2(__float2half_rn(__fmul_rn(f.x, rstd)),
+                                          __float2half_rn(__fmul_rn(f.y, rstd)));
+        h[e] = __hmul2(n2, g2[e]);
+        const float2 y = __half22float2(h[e]);
+        amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
+      }
+      row[j] = v;
+    }
+    amax = warp_max(amax);
+    if (lane == 0) sh_max[m * nw + warp] = amax;
+  }
+  __syncthreads();
+  for (int m = 0; m < p.M; ++m) {
+    float scale;
+    if (p.norm_static != nullptr) {
+      scale = __ldg(p.norm_static);
+    } else {
+      float mx = 0.f;
+      for (int w = 0; w < nw; ++w) mx = fmaxf(mx, sh_max[m * nw + w]);
+      scale = dyn_scale(mx);
+      if (tid == 0 && p.norm_scale_out != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
+        p.norm_scale_out[m] = scale;
+    }
+    if (tid == 0) scale_sh[m] = scale;
+    uint4* row = xs + (m * p.xs_stride) / 8;
+    for (int j = tid; j < nvec; j += nt) {
+      uint4 v = row[j];
+      uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 y = __half22float2(u32_as_h2(u[e]));
+        const uint16_t code = cvt_e4m3x2(__fdiv_rn(y.x, scale), __fdiv_rn(y.y, scale));
+        uint32_t h;
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(code));
+        u[e] = h;
+      }
+      row[j] = v;
+    }
+  }
+  __syncthreads();
+}
+
+template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact, bool kNorm = false>
 __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N * WARPS_K))
     w4a16_gemv_kernel(const GemvParams p) {
   constexpr int kWarps = WARPS_N * WARPS_K;
@@ -438,6 +531,7 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   extern __shared__ uint4 xs_smem[];
   // Per warp: two tiles x four fragment values x 32 lanes.
   __shared__ float red[kWarps * 2 * 4 * 32];
+  __shared__ float norm_scale_sh[kNorm ? 8 : 1];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wn = warp / WARPS_K, wk = warp % WARPS_K;
@@ -537,6 +631,7 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
     asm volatile("cp.async.wait_all;" ::: "memory");
   }
   __syncthreads();
+  if constexpr (kNorm) norm_quant_staged(p, xs_smem, red, norm_scale_sh);
 
   float acc[2][2][4] = {};
   float y[2][4] = {};
@@ -632,13 +727,13 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   }
   if (!store) return;
 
-  if (p.x_scale != nullptr) {  // FP8 activations: the per-token scale, before the bias
+  if (kNorm || p.x_scale != nullptr) {  // FP8 activations: the per-token scale, before the bias
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int m = min(2 * L.c + (r & 1), p.M - 1);
-        v[t][r] *= __ldg(p.x_scale + m * p.x_scale_stride);
+        v[t][r] *= kNorm ? norm_scale_sh[m] : __ldg(p.x_scale + m * p.x_scale_stride);
       }
   }
   // Fragment value r of tile t: row 4q + 2t (r < 2) or 4q + 2t + 1 (r >= 2), token 2c + (r & 1).
@@ -681,10 +776,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   y[m * ldy + n] = __float2half_rn(s);
 }
 
-template <int WN, int WK, bool kCluster, bool kFact>
+template <int WN, int WK, bool kCluster, bool kFact, bool kNorm = false>
 int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
                         cudaStream_t stream, bool pdl) {
-  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact>;
+  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact, kNorm>;
   // Static (the reduction buffer, 1 KB per warp) plus dynamic shared memory above the default
   // 48 KB needs the opt-in limit raised.
   constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 4 * 32 * sizeof(float);
@@ -725,17 +820,17 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
   return TF_OK;
 }
 
-template <bool kCluster, bool kFact>
+template <bool kCluster, bool kFact, bool kNorm = false>
 int launch_gemv_shape(const LinearPlan& plan, const GemvParams& p, size_t smem, cudaStream_t st,
                       bool pdl) {
   switch (plan.warps_k) {
-    case 1: return launch_gemv_variant<8, 1, kCluster, kFact>(plan, p, smem, st, pdl);
-    case 2: return launch_gemv_variant<4, 2, kCluster, kFact>(plan, p, smem, st, pdl);
-    case 4: return launch_gemv_variant<2, 4, kCluster, kFact>(plan, p, smem, st, pdl);
-    case 8: return launch_gemv_variant<1, 8, kCluster, kFact>(plan, p, smem, st, pdl);
+    case 1: return launch_gemv_variant<8, 1, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
+    case 2: return launch_gemv_variant<4, 2, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
+    case 4: return launch_gemv_variant<2, 4, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
+    case 8: return launch_gemv_variant<1, 8, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
     case 16:
       if constexpr (kCluster) return TF_ERR_INVALID_ARG;
-      else return launch_gemv_variant<1, 16, false, kFact>(plan, p, smem, st, pdl);
+      else return launch_gemv_variant<1, 16, false, kFact, kNorm>(plan, p, smem, st, pdl);
     default: return TF_ERR_INVALID_ARG;
   }
 }
@@ -772,6 +867,10 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   p.peer_world = 0;
   p.peer_rank = 0;
   p.peer_ctl = nullptr;
+  p.norm_w = reinterpret_cast<const __half*>(a.norm_w);
+  p.norm_eps = a.norm_eps;
+  p.norm_static = a.norm_static;
+  p.norm_scale_out = a.norm_scale_out;
   if (a.peers != nullptr) {
     const TfPeerSet& ps = *a.peers;
     const PeerLayout lay = peer_layout(ps.world, ps.max_m, ps.max_n);
@@ -792,6 +891,12 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   // tensor-core sums; other group sizes dequantize every weight.
   const bool fact = a.group_size == kKB;
   int st;
+  if (a.norm_w != nullptr) {
+    // The fused RMSNorm needs every CTA to hold whole rows (checked by the caller).
+    if (plan.cluster != 1 || plan.split_k != 1 || a.peers != nullptr) return TF_ERR_UNSUPPORTED;
+    return fact ? launch_gemv_shape<false, true, true>(plan, p, smem, stream, pdl)
+                : launch_gemv_shape<false, false, true>(plan, p, smem, stream, pdl);
+  }
   if (plan.cluster > 1)
     st = fact ? launch_gemv_shape<true, true>(plan, p, smem, stream, pdl)
               : launch_gemv_shape<true, false>(plan, p, smem, stream, pdl);

@@ -280,6 +280,78 @@ def _w4a16_linear_fp8_fake(xq, x_scale, qweight_t, scales, qzeros, bias, group_s
                        device=xq.device)
 
 
+@torch.library.custom_op("tokenforge::rmsnorm_fp8_w4a16_linear", mutates_args=())
+def rmsnorm_fp8_w4a16_linear(
+    x: torch.Tensor,
+    norm_weight: torch.Tensor,
+    eps: float,
+    scale: torch.Tensor | None,
+    qweight_t: torch.Tensor,
+    scales: torch.Tensor,
+    qzeros: torch.Tensor,
+    bias: torch.Tensor | None,
+    group_size: int,
+) -> torch.Tensor:
+    """``w4a16_linear_fp8(*rmsnorm_fp8_quant(x, norm_weight, eps, scale), ...)`` in one decode
+    kernel (M <= 8 tokens, layers whose decode plan keeps K in one CTA): the normalised and
+    quantised activations stay in shared memory, and y is bit-identical to the two-op path.
+    Other sizes run the two ops (both on the GPU). No reference counterpart."""
+    k = x.shape[-1]
+    n = qweight_t.shape[0]
+    out_shape = (*x.shape[:-1], n)
+    x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if m == 0:
+        return torch.empty(out_shape, dtype=torch.float16, device=x.device)
+    if x.dtype != torch.float16 or norm_weight.dtype != torch.float16:
+        raise TypeError("x and norm_weight must be fp16")
+    if tuple(norm_weight.shape) != (k,):
+        raise ValueError(f"norm_weight shape {tuple(norm_weight.shape)} != {(k,)}")
+    if scale is not None and (scale.numel() != 1 or scale.dtype != torch.float32):
+        raise ValueError("static scale must be a single fp32 element")
+    _check_inputs(x2, qweight_t, scales, qzeros, group_size)
+    for name, t in (("x", x), ("norm_weight", norm_weight), ("qweight_t", qweight_t),
+                    ("scales", scales), ("qzeros", qzeros)):
+        _require(t, name)
+    if bias is not None:
+        _require(bias, "bias")
+        if tuple(bias.shape) != (n,) or bias.dtype != torch.float16:
+            raise ValueError(f"bias must be fp16 [{n}]")
+        bias = bias.contiguous()
+    if m <= 8:
+        xc = x2
+        if xc.stride(-1) != 1 or xc.data_ptr() % _VEC or (m > 1 and xc.stride(0) % 8):
+            xc = x2.contiguous()
+            if xc.data_ptr() % _VEC:
+                xc = xc.clone()
+        nw = norm_weight.contiguous()
+        if nw.data_ptr() % _VEC:
+            nw = nw.clone()
+        if scale is not None:
+            _require(scale, "scale")
+        y = torch.empty((m, n), dtype=torch.float16, device=x.device)
+        with torch.cuda.device(x.device):
+            status = _lib.lib().tf_rmsnorm_fp8_w4a16_linear(
+                xc.data_ptr(), m, k, xc.stride(0) if m > 1 else k, nw.data_ptr(), float(eps),
+                _lib.ptr(scale), None, qweight_t.data_ptr(), scales.data_ptr(),
+                qzeros.data_ptr(), _lib.ptr(bias), n, group_size, y.data_ptr(), n, None, 0,
+                _lib.stream_ptr(x.device),
+            )  # fmt: skip
+        if status == _lib.TF_OK:
+            return y.reshape(out_shape)
+        if status != _lib.TF_ERR_UNSUPPORTED:
+            _lib.check("tf_rmsnorm_fp8_w4a16_linear", status)
+    q, s = rmsnorm_fp8_quant(x2, norm_weight, eps, scale)
+    return w4a16_linear_fp8(q, s, qweight_t, scales, qzeros, bias, group_size).reshape(out_shape)
+
+
+@rmsnorm_fp8_w4a16_linear.register_fake
+def _rmsnorm_fp8_w4a16_linear_fake(x, norm_weight, eps, scale, qweight_t, scales, qzeros, bias,  # type: ignore[no-untyped-def]
+                                   group_size):
+    return torch.empty((*x.shape[:-1], qweight_t.shape[0]), dtype=torch.float16,
+                       device=x.device)
+
+
 def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
     """``gate_up [..., 2I] fp16 -> silu(gate) * up [..., I] fp16`` (fp32 inside, one rounding)."""
     if gate_up.dtype != torch.float16:
