@@ -393,13 +393,15 @@ def run_reference(args: argparse.Namespace) -> None:
 # ----------------------------------------------------------------------------- block stack (config 4)
 
 
-def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], steps: int) -> dict:
+def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], steps: int,
+                 fuse_norm: bool = True) -> dict:
     """the Qwen2.5-7B-shaped quantized block stack on the sweep's 28 layers of
     weights. Per layer: rmsnorm_fp8_quant of the fp16 residual -> W4A16 qkv on the e4m3
     activations -> the v slice (512 channels) repeated 7x stands in for attention -> W4A16 o ->
     residual add -> rmsnorm_fp8_quant -> W4A16 gate_up on e4m3 -> SiLU * up -> W4A16 down ->
     residual add. One step = the 28 layers on M tokens, replayed as a CUDA graph; tokens/s =
-    M / step time."""
+    M / step time. With fuse_norm, each RMSNorm + quant + linear pair is the one fused op
+    (rmsnorm_fp8_w4a16_linear: one kernel at decode sizes, bit-identical; two ops otherwise)."""
     import tokenforge_b200.ops as ops
 
     gen = torch.Generator(device=device).manual_seed(123)
@@ -408,24 +410,28 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
     out: dict[str, object] = {
         "metric": "Qwen2.5-7B quantized block stack tokens/s (config 4, 28 layers, TP=1)",
         "unit": "tokens/s",
+        "fused_norm_linear": fuse_norm,
         "per_m": {},
     }
     for m in ms:
         h0 = torch.randn((m, HIDDEN), generator=gen, device=device).to(torch.float16)
 
+        def norm_linear(h: torch.Tensor, gamma: torch.Tensor, wt) -> torch.Tensor:  # type: ignore[no-untyped-def]
+            if fuse_norm:
+                return torch.ops.tokenforge.rmsnorm_fp8_w4a16_linear(
+                    h, gamma, 1e-6, None, wt.qweight_t, wt.scales, wt.qzeros, None, G)
+            q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma, 1e-6, None)
+            return torch.ops.tokenforge.w4a16_linear_fp8(q, sc, wt.qweight_t, wt.scales,
+                                                         wt.qzeros, None, G)
+
         def step() -> None:
             h = h0
             for row, gamma in zip(sweep.layers, gammas):
                 w = {name: wt for name, wt, _ in row}
-                q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma[0], 1e-6, None)
-                qkv = torch.ops.tokenforge.w4a16_linear_fp8(
-                    q, sc, w["qkv"].qweight_t, w["qkv"].scales, w["qkv"].qzeros, None, G)
+                qkv = norm_linear(h, gamma[0], w["qkv"])
                 v = qkv[:, 4096:].repeat(1, 7)
                 h = h + ops.w4a16_gemm(v, w["o"].qweight_t, w["o"].scales, w["o"].qzeros, G)
-                q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma[1], 1e-6, None)
-                gu = torch.ops.tokenforge.w4a16_linear_fp8(
-                    q, sc, w["gate_up"].qweight_t, w["gate_up"].scales, w["gate_up"].qzeros,
-                    None, G)
+                gu = norm_linear(h, gamma[1], w["gate_up"])
                 a = ops.silu_mul(gu)
                 h = h + ops.w4a16_gemm(a, w["down"].qweight_t, w["down"].scales,
                                        w["down"].qzeros, G)
@@ -589,6 +595,10 @@ def main() -> None:
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
     ap.add_argument("--skip-block", action="store_true", help="omit the config-4 block-stack leg")
+    ap.add_argument("--block-ms", type=str, default="1,64,2048",
+                    help="token counts M of the config-4 block-stack leg")
+    ap.add_argument("--no-fuse-norm", action="store_true",
+                    help="block stack: separate RMSNorm+FP8 and linear launches")
     ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
                     help="restrict the sweep to these layer types (profiling a small case)")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -724,7 +734,8 @@ def main() -> None:
         extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None
     if world == 1 and full and not args.skip_block:
-        block = block_metric(sweep, device, (1, 64, 2048), max(3, args.steps // 2))
+        block = block_metric(sweep, device, tuple(int(v) for v in args.block_ms.split(",")),
+                             max(3, args.steps // 2), fuse_norm=not args.no_fuse_norm)
     cpu = None
     if rank == 0 and world == 1 and full and not args.skip_cpu:
         cpu = cpu_baseline(args.m, min_seconds=10.0)

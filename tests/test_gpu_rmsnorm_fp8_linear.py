@@ -41,14 +41,16 @@ def _fused(x, gamma, scale, w, bias):  # type: ignore[no-untyped-def]
                                                          w.scales, w.qzeros, bias, w.group_size)
 
 
-def _fused_status(x, gamma, w, scale_out):  # type: ignore[no-untyped-def]
+def _fused_status(x, gamma, w, scale_out, static=None, bias=None):  # type: ignore[no-untyped-def]
+    """The fused kernel through the C ABI at any M (the torch op takes it for one token only)."""
     m, k = x.shape
     n = w.qweight_t.shape[0]
     y = torch.empty((m, n), dtype=torch.float16, device=x.device)
     st = _lib.lib().tf_rmsnorm_fp8_w4a16_linear(
-        x.data_ptr(), m, k, k, gamma.data_ptr(), EPS, None, scale_out.data_ptr(),
-        w.qweight_t.data_ptr(), w.scales.data_ptr(), w.qzeros.data_ptr(), None, n, w.group_size,
-        y.data_ptr(), n, None, 0, _lib.stream_ptr(x.device))
+        x.data_ptr(), m, k, k, gamma.data_ptr(), EPS, _lib.ptr(static), _lib.ptr(scale_out),
+        w.qweight_t.data_ptr(), w.scales.data_ptr(), w.qzeros.data_ptr(), _lib.ptr(bias), n,
+        w.group_size, y.data_ptr(), n, None, 0, _lib.stream_ptr(x.device))
+    torch.cuda.synchronize()
     return st, y
 
 
@@ -67,14 +69,14 @@ def test_fused_is_bit_identical_to_the_two_op_path(m: int, n: int, k: int,
     plan = launch_plan(m, n, k, 128)
     single_pass = plan.kernel == "gemv" and plan.split_k == 1 and plan.cluster == 1
     scale_out = torch.full((m,), -1.0, dtype=torch.float32, device=device)
-    st, y = _fused_status(x, gamma, w, scale_out)
+    st, y = _fused_status(x, gamma, w, scale_out, bias=b)
     if not single_pass:
         assert st == _lib.TF_ERR_UNSUPPORTED
         return
     assert st == _lib.TF_OK
     _, s_ref = torch.ops.tokenforge.rmsnorm_fp8_quant(x, gamma, EPS, None)
     assert torch.equal(scale_out, s_ref.reshape(-1))
-    assert torch.equal(y, _two_op(x, gamma, None, w, None))
+    assert torch.equal(y, _two_op(x, gamma, None, w, b))
 
 
 @pytest.mark.parametrize("g", [32, 64])
@@ -86,6 +88,9 @@ def test_fused_group_sizes_and_static_scale(g: int, m: int, device: torch.device
     static = torch.tensor([0.05], dtype=torch.float32, device=device)
     for scale in (None, static):
         assert torch.equal(_fused(x, gamma, scale, w, None), _two_op(x, gamma, scale, w, None))
+        st, y = _fused_status(x, gamma, w, None, static=scale)
+        assert st == _lib.TF_OK
+        assert torch.equal(y, _two_op(x, gamma, scale, w, None))
 
 
 def test_fused_non_finite_rows_match(device: torch.device) -> None:
@@ -94,7 +99,8 @@ def test_fused_non_finite_rows_match(device: torch.device) -> None:
     x, gamma = _inputs(m, k, 13, device, outliers=False)
     x[1, 7] = float("inf")
     x[2, 100] = float("nan")
-    y_f = _fused(x, gamma, None, w, None)
+    st, y_f = _fused_status(x, gamma, w, None)
+    assert st == _lib.TF_OK
     y_t = _two_op(x, gamma, None, w, None)
     assert torch.equal(torch.isnan(y_f), torch.isnan(y_t))
     fin = ~torch.isnan(y_t)

@@ -292,10 +292,12 @@ def rmsnorm_fp8_w4a16_linear(
     bias: torch.Tensor | None,
     group_size: int,
 ) -> torch.Tensor:
-    """``w4a16_linear_fp8(*rmsnorm_fp8_quant(x, norm_weight, eps, scale), ...)`` in one decode
-    kernel (M <= 8 tokens, layers whose decode plan keeps K in one CTA): the normalised and
+    """``w4a16_linear_fp8(*rmsnorm_fp8_quant(x, norm_weight, eps, scale), ...)``. For one token
+    on a layer whose decode plan keeps K in one CTA, this is one kernel: the normalised and
     quantised activations stay in shared memory, and y is bit-identical to the two-op path.
-    Other sizes run the two ops (both on the GPU). No reference counterpart."""
+    Otherwise the two ops run (both on the GPU): every CTA of the fused kernel normalises all
+    M rows itself, which on B200 costs more than the saved launch from M = 2 on (measured in
+    the block stack: +2.7% tokens/s at M = 1, -21% at M = 8). No reference counterpart."""
     k = x.shape[-1]
     n = qweight_t.shape[0]
     out_shape = (*x.shape[:-1], n)
@@ -318,9 +320,9 @@ def rmsnorm_fp8_w4a16_linear(
         if tuple(bias.shape) != (n,) or bias.dtype != torch.float16:
             raise ValueError(f"bias must be fp16 [{n}]")
         bias = bias.contiguous()
-    if m <= 8:
+    if m == 1:
         xc = x2
-        if xc.stride(-1) != 1 or xc.data_ptr() % _VEC or (m > 1 and xc.stride(0) % 8):
+        if xc.stride(-1) != 1 or xc.data_ptr() % _VEC:
             xc = x2.contiguous()
             if xc.data_ptr() % _VEC:
                 xc = xc.clone()
@@ -332,7 +334,7 @@ def rmsnorm_fp8_w4a16_linear(
         y = torch.empty((m, n), dtype=torch.float16, device=x.device)
         with torch.cuda.device(x.device):
             status = _lib.lib().tf_rmsnorm_fp8_w4a16_linear(
-                xc.data_ptr(), m, k, xc.stride(0) if m > 1 else k, nw.data_ptr(), float(eps),
+                xc.data_ptr(), m, k, k, nw.data_ptr(), float(eps),
                 _lib.ptr(scale), None, qweight_t.data_ptr(), scales.data_ptr(),
                 qzeros.data_ptr(), _lib.ptr(bias), n, group_size, y.data_ptr(), n, None, 0,
                 _lib.stream_ptr(x.device),
