@@ -1,0 +1,118 @@
+"""AWQ checkpoint loader, host side: the safetensors reader against files written by the
+`safetensors` package, sharded checkpoints, the quantisation-config rules and the q/k/v and
+gate/up fusion checked nibble by nibble with the oracle's unpack."""
+
+from __future__ import annotations
+
+import json
+import struct
+
+import pytest
+import torch
+
+from oracle import oracle
+from tests.awq_checkpoint import HIDDEN, INTER, KV, write_checkpoint
+from tokenforge_b200.checkpoint import (
+    AWQConfig, Checkpoint, CheckpointError, SafetensorsFile, fused_awq_tensors, num_layers,
+)
+
+safetensors_torch = pytest.importorskip("safetensors.torch")
+
+
+def test_reader_matches_the_reference_writer(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    gen = torch.Generator().manual_seed(0)
+    tensors = {
+        "f16": torch.randn((3, 5), generator=gen).half(),
+        "bf16": torch.randn(4, generator=gen).bfloat16(),
+        "f32": torch.tensor(1.5),
+        "i32": torch.randint(-(2**31), 2**31 - 1, (2, 3), generator=gen, dtype=torch.int32),
+        "i64": torch.arange(3, dtype=torch.int64) - 7,
+        "u8": torch.empty(0, dtype=torch.uint8),
+        "b": torch.tensor([True, False, True]),
+    }
+    path = tmp_path / "t.safetensors"
+    safetensors_torch.save_file(tensors, str(path), metadata={"format": "pt", "note": "x"})
+    f = SafetensorsFile(path)
+    assert sorted(f.keys()) == sorted(tensors)
+    assert f.metadata == {"format": "pt", "note": "x"}
+    for name, t in tensors.items():
+        got = f.get(name)
+        assert got.dtype == t.dtype and got.shape == t.shape
+        assert torch.equal(got, t)
+    # Views are copy-on-write: writing one leaves the file as it was.
+    f.get("i32").zero_()
+    assert torch.equal(SafetensorsFile(path).get("i32"), tensors["i32"])
+
+
+def test_reader_rejects_corrupt_files(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    p = tmp_path / "short.safetensors"
+    p.write_bytes(b"\x01\x02")
+    with pytest.raises(CheckpointError, match="too short"):
+        SafetensorsFile(p)
+    header = json.dumps({"a": {"dtype": "F16", "shape": [4], "data_offsets": [0, 8]}}).encode()
+    p = tmp_path / "trunc.safetensors"
+    p.write_bytes(struct.pack("<Q", len(header)) + header + b"\0" * 4)  # 4 of 8 data bytes
+    with pytest.raises(CheckpointError, match="data_offsets"):
+        SafetensorsFile(p)
+    header = json.dumps({"a": {"dtype": "F8_E9", "shape": [1], "data_offsets": [0, 1]}}).encode()
+    p = tmp_path / "dtype.safetensors"
+    p.write_bytes(struct.pack("<Q", len(header)) + header + b"\0")
+    with pytest.raises(CheckpointError, match="unsupported dtype"):
+        SafetensorsFile(p)
+
+
+@pytest.mark.parametrize("shards", [1, 3])
+def test_checkpoint_reads_single_and_sharded_models(tmp_path, shards: int) -> None:  # type: ignore[no-untyped-def]
+    tensors = write_checkpoint(tmp_path, layers=3, shards=shards)
+    ck = Checkpoint(tmp_path)
+    assert sorted(ck.keys()) == sorted(tensors)
+    for name in ("model.layers.2.mlp.down_proj.qweight", "model.layers.0.self_attn.q_proj.bias"):
+        assert torch.equal(ck.get(name), tensors[name])
+    assert num_layers(ck) == 3
+    with pytest.raises(KeyError, match="no tensor"):
+        ck.get("model.layers.3.mlp.down_proj.qweight")
+
+
+def test_quant_config_rules(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    autoawq = {"zero_point": True, "q_group_size": 128, "w_bit": 4, "version": "GEMM"}
+    assert AWQConfig.from_dict(autoawq) == AWQConfig(4, 128, True, "gemm")
+    hf = {"quant_method": "awq", "bits": 4, "group_size": 64, "zero_point": True,
+          "version": "gemm", "modules_to_not_convert": ["visual"]}
+    assert AWQConfig.from_dict(hf).modules_to_not_convert == ("visual",)
+    (tmp_path / "config.json").write_text(json.dumps({"quantization_config": hf}))
+    assert AWQConfig.from_dir(tmp_path).group_size == 64
+    for bad, match in (({**autoawq, "w_bit": 8}, "8-bit"), ({**autoawq, "zero_point": False}, "zero points"),
+                       ({**autoawq, "q_group_size": 96}, "group size"), ({**autoawq, "version": "GEMV"}, "packing"),
+                       ({**hf, "quant_method": "gptq"}, "not AWQ")):
+        with pytest.raises(CheckpointError, match=match):
+            AWQConfig.from_dict(bad)
+
+
+def test_fusion_concatenates_projections_along_n(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    tensors = write_checkpoint(tmp_path, layers=1, g=64)
+    ck = Checkpoint(tmp_path)
+    pre = "model.layers.0.self_attn."
+    qw, qz, sc, bias = fused_awq_tensors(ck, [pre + p for p in ("q_proj", "k_proj", "v_proj")])
+    n = HIDDEN + 2 * KV
+    assert qw.shape == (HIDDEN, n // 8) and qz.shape == (HIDDEN // 64, n // 8)
+    assert sc.shape == (HIDDEN // 64, n) and bias is not None and bias.shape == (n,)
+    # Nibble by nibble: the fused matrix's integer weights are the projections' side by side.
+    ints = oracle.unpack_int4(qw)
+    parts = [oracle.unpack_int4(tensors[pre + p + ".qweight"]) for p in ("q_proj", "k_proj", "v_proj")]
+    assert torch.equal(ints, torch.cat(parts, dim=1))
+    zs = oracle.unpack_int4(qz)
+    assert torch.equal(zs, torch.cat([oracle.unpack_int4(tensors[pre + p + ".qzeros"])
+                                      for p in ("q_proj", "k_proj", "v_proj")], dim=1))
+    gu = fused_awq_tensors(ck, ["model.layers.0.mlp.gate_proj", "model.layers.0.mlp.up_proj"])
+    assert gu[0].shape == (HIDDEN, 2 * INTER // 8) and gu[3] is None
+
+
+def test_fusion_rejects_inconsistent_projections(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    write_checkpoint(tmp_path, layers=1)
+    ck = Checkpoint(tmp_path)
+    with pytest.raises(CheckpointError, match="disagree on K"):
+        fused_awq_tensors(ck, ["model.layers.0.mlp.gate_proj", "model.layers.0.mlp.down_proj"])
+    with pytest.raises(CheckpointError, match="bias present on some"):
+        fused_awq_tensors(ck, ["model.layers.0.self_attn.q_proj", "model.layers.0.self_attn.o_proj"])
+    with pytest.raises(CheckpointError, match="no tensor"):
+        fused_awq_tensors(ck, ["model.layers.0.mlp.missing_proj"])
