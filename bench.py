@@ -595,6 +595,8 @@ def main() -> None:
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the GEMM M=1024 leg")
     ap.add_argument("--skip-block", action="store_true", help="omit the config-4 block-stack leg")
+    ap.add_argument("--skip-aux", action="store_true",
+                    help="omit the AWQ repack and RMSNorm+FP8 legs (configs 1 and 2)")
     ap.add_argument("--block-ms", type=str, default="1,64,2048",
                     help="token counts M of the config-4 block-stack leg")
     ap.add_argument("--no-fuse-norm", action="store_true",
@@ -729,7 +731,7 @@ def main() -> None:
         gemm = gemm_metric(device, tuple(sorted(gemm_ms)),
                            max(3, args.steps // 2), 3, pk, src, headline_m=args.gemm_m)
     extra = {}
-    if world == 1 and full and not args.skip_gemm:
+    if world == 1 and full and not args.skip_aux:
         extra["repack"] = repack_metric(device, max(3, args.steps // 2), pk)
         extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None

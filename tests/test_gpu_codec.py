@@ -32,7 +32,7 @@ def _same_fp16(a: torch.Tensor, b: torch.Tensor) -> bool:
 
 @pytest.mark.parametrize(("k", "n"), [(8, 8), (24, 8), (64, 200), (256, 64), (128, 1000),
                                       (896, 1152), (3584, 4608), (3584, 37888), (18944, 3584),
-                                      (3584 + 64, 3584)])
+                                      (3584 + 64, 3584), (2056, 1088), (1032, 96 * 8)])
 def test_repack_bit_exact(k: int, n: int, device: torch.device) -> None:
     gen = torch.Generator().manual_seed(k * 131 + n)
     qweight = torch.randint(-(2**31), 2**31 - 1, (k, n // 8), generator=gen, dtype=torch.int32)

@@ -174,3 +174,23 @@ def test_rejects_bad_inputs(device: torch.device) -> None:
         rmsnorm_fp8_quant_2d(x.to(device), w[:64].to(device), EPS)
     with pytest.raises(ValueError, match="single fp32"):
         rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS, torch.ones(2, device=device))
+
+
+@pytest.mark.parametrize("h", [1032, 2048, 3072, 3584, 4096])
+@pytest.mark.parametrize("t", [1024, 1029, 2500])
+def test_many_rows(t: int, h: int, device: torch.device) -> None:
+    """Thousands of rows of 1025-4096 elements (several waves of CTAs, ragged T): codes and
+    scales bit-exact against the oracle, dynamic and static scale."""
+    gen = torch.Generator().manual_seed(t * 7 + h)
+    x = torch.randn((t, h), generator=gen)
+    x[:, torch.randperm(h, generator=gen)[:8]] *= 20
+    x = x.to(torch.float16)
+    w = (1 + 0.1 * torch.randn(h, generator=gen)).to(torch.float16)
+    q, s = rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS)
+    q_ref, s_ref = oracle.rmsnorm_fp8(x, w, EPS)
+    assert torch.equal(_codes(q), q_ref.to(torch.int16))
+    assert torch.equal(s.cpu(), s_ref)
+    static = torch.tensor([0.05], dtype=torch.float32)
+    q, _ = rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS, static.to(device))
+    q_ref, _ = oracle.rmsnorm_fp8(x, w, EPS, static)
+    assert torch.equal(_codes(q), q_ref.to(torch.int16))

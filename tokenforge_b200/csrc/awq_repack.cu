@@ -141,6 +141,61 @@ __global__ void __launch_bounds__(128) awq_repack_tiled_kernel(const uint32_t* _
   }
 }
 
+// AWQ_ORDER as a compile-time function, so that fully unrolled loops index registers.
+__device__ __forceinline__ constexpr int awq_order(int j) { return j < 4 ? 2 * j : 2 * j - 7; }
+
+// The same tile, loaded 16 bytes at a time (input row stride a multiple of four words, 16-byte
+// aligned): thread (cq, g) takes column words 4cq .. 4cq+3 of row groups g and g + 16 (eight
+// input rows each), all sixteen 16-byte loads in flight before the first transpose, so a CTA
+// keeps its whole 32 KB input tile in flight (the one-word variant above has 32 B per thread
+// outstanding). A warp's load covers four rows x 128 contiguous bytes; the shared-memory writes
+// (bank (4cq + cc + g) mod 32) do not conflict; the output phase is the one above.
+__global__ void __launch_bounds__(128) awq_repack_tiled_v4_kernel(const uint32_t* __restrict__ in,
+                                                                  int64_t rows, int64_t cols8,
+                                                                  uint32_t* __restrict__ out) {
+  __shared__ uint32_t tile[kTileRows][kTileW + 1];
+  const int cq = threadIdx.x & 7, g = threadIdx.x >> 3;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kTileW + 4 * cq;
+  const int64_t out_words = rows / 8;
+  const int64_t kw_base = static_cast<int64_t>(blockIdx.y) * kTileW;
+  const int64_t row_vecs = cols8 / 4;
+  uint4 ld[2][8];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int64_t kw = kw_base + g + 16 * h;
+    const bool ok = c0 < cols8 && kw < out_words;  // cols8 % 4 == 0: the quad is all in or out
+    const uint4* src = reinterpret_cast<const uint4*>(in + kw * 8 * cols8 + c0);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) ld[h][r] = ok ? ldg_stream_v4(src + r * row_vecs) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = reinterpret_cast<const uint32_t*>(&ld[h][awq_order(j)])[cc];
+      transpose8x8_nibbles(w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tile[32 * awq_order(i) + 4 * cq + cc][g + 16 * h] = w[i];
+    }
+  }
+  __syncthreads();
+  const int sub = threadIdx.x & 7, rsub = threadIdx.x >> 3;
+  for (int r = rsub; r < kTileRows; r += 16) {
+    const int64_t orow = static_cast<int64_t>(blockIdx.x) * kTileRows + r;
+    if (orow >= cols8 * 8) break;
+    const int64_t kw = kw_base + 4 * sub;
+    uint32_t* dst = out + orow * out_words + kw;
+    const uint32_t* srow = &tile[32 * (r & 7) + (r >> 3)][4 * sub];
+    if (kw + 4 <= out_words && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(srow[0], srow[1], srow[2], srow[3]);
+    } else {
+      for (int e = 0; e < 4 && kw + e < out_words; ++e) dst[e] = srow[e];
+    }
+  }
+}
+
 int launch_repack(const int32_t* in, int64_t rows, int64_t cols, int32_t* out,
                   cudaStream_t stream) {
   // rows: the packed-across dimension of the output (K for repack); cols: logical columns.
@@ -152,6 +207,11 @@ int launch_repack(const int32_t* in, int64_t rows, int64_t cols, int32_t* out,
   if (out_words >= kTileW && cols8 >= kTileW) {
     const dim3 tgrid(static_cast<unsigned>(cdiv(cols8, kTileW)),
                      static_cast<unsigned>(cdiv(out_words, kTileW)));
+    if (tgrid.y <= 65535u && cols8 % 4 == 0 && aligned16(in)) {
+      awq_repack_tiled_v4_kernel<<<tgrid, 128, 0, stream>>>(
+          reinterpret_cast<const uint32_t*>(in), rows, cols8, reinterpret_cast<uint32_t*>(out));
+      return check_launch();
+    }
     if (tgrid.y <= 65535u) {
       awq_repack_tiled_kernel<<<tgrid, 128, 0, stream>>>(
           reinterpret_cast<const uint32_t*>(in), rows, cols8, reinterpret_cast<uint32_t*>(out));
