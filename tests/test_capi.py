@@ -58,10 +58,23 @@ def test_decode_sizes_use_the_gemv(m: int) -> None:
     assert plan.tile_m == 8
 
 
-@pytest.mark.parametrize("m", [9, 16, 64, 129, 1024, 4096, 5000])
+@pytest.mark.parametrize("m", [17, 32, 64, 129, 1024, 4096, 5000])
 def test_prefill_sizes_use_a_gemm(m: int) -> None:
     plan = launch_plan(m, 37888, 3584, 128)
     assert plan.kernel in ("tcgen05_gemm", "mma_gemm")
+
+
+@pytest.mark.parametrize("m", [9, 12, 16])
+def test_batched_decode_uses_the_16_token_gemv(m: int) -> None:
+    """M = 9..16 with group size 128: the GEMV with two 8-token n-tiles (8-warp CTAs, two per
+    SM, activations at most 96 KB per CTA); other group sizes take a GEMM."""
+    for n, k in [(4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944)]:
+        plan = launch_plan(m, n, k, 128)
+        assert plan.kernel == "gemv" and plan.tile_m == 16 and plan.m_bucket == 16
+        assert plan.warps_k in (1, 2, 4, 8)  # no 16-warp CTA at 16 tokens
+        per_split = -(-(-(-k // 128)) // plan.split_k)
+        assert 2 * m * (per_split * 128 + 8) <= 96 * 1024
+    assert launch_plan(m, 4608, 3584, 64).kernel in ("tcgen05_gemm", "mma_gemm")
 
 
 @pytest.mark.parametrize(("n", "k"), [(4608, 3584), (3584, 3584), (37888, 3584), (3584, 18944),
@@ -95,7 +108,7 @@ def test_decode_plan_fills_the_gpu_without_a_reduce_launch() -> None:
         assert plan.split_k == plan.cluster  # any K split is reduced inside the CTA or cluster
 
 
-@pytest.mark.parametrize(("m", "n", "k"), [(1024, 3584, 18944), (64, 3584, 18944), (16, 37888, 3584)])
+@pytest.mark.parametrize(("m", "n", "k"), [(1024, 3584, 18944), (64, 3584, 18944), (32, 37888, 3584)])
 def test_tensor_core_plan_splits_k_to_fill_the_gpu(m: int, n: int, k: int) -> None:
     plan = launch_plan(m, n, k, 128)
     assert plan.kernel == "tcgen05_gemm"

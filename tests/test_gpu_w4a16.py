@@ -240,3 +240,52 @@ def test_drop_in_extension_module(device: torch.device) -> None:
     wd = w.to(device)
     y = _C.w4a16_gemv(x.to(device), wd.qweight_t, wd.scales, wd.qzeros, b.to(device), G)
     _check(y, x, w, b)
+
+
+@pytest.mark.parametrize(("m", "n", "k"), [(12, 3584, 18944), (16, 3584, 18944), (9, 256, 65536),
+                                           (16, 1000, 1024), (13, 4608, 3584)])
+def test_16_token_gemv_split_k_paths(m: int, n: int, k: int, device: torch.device) -> None:
+    """M = 9..16 on the 16-token GEMV: K split inside a cluster and across clusters (fp32
+    partials + the reduce kernel), ragged N, bias."""
+    plan = launch_plan(m, n, k, G)
+    assert plan.kernel == "gemv" and plan.tile_m == 16
+    w = cases.layer_weights(n, k, 0)
+    b = cases.bias(n, 0)
+    x = cases.activations(m, k, 0)
+    y = _linear(x.to(device), w.to(device), b.to(device))
+    _check(y, x, w, b)
+
+
+def test_16_token_gemv_non_finite_in_either_n_tile(device: torch.device) -> None:
+    w = cases.layer_weights(64, 256, 0)
+    x = cases.activations(14, 256, 0)
+    x[2, 5] = float("inf")     # first n-tile (tokens 0-7)
+    x[10, 7] = float("-inf")   # second n-tile (tokens 8-15)
+    x[12, 9] = float("nan")
+    ref16 = oracle.w4a16_reference(x, w.qweight_t, w.scales, w.qzeros, G).to(torch.float16)
+    y = _linear(x.to(device), w.to(device)).cpu()
+    assert torch.equal(torch.isnan(y), torch.isnan(ref16))
+    assert torch.equal(torch.isposinf(y), torch.isposinf(ref16))
+    assert torch.equal(torch.isneginf(y), torch.isneginf(ref16))
+    clean = [i for i in range(14) if i not in (2, 10, 12)]
+    assert bool(torch.isfinite(y[clean]).all())
+    _check(y[clean].to(device), x[clean], w)
+
+
+@pytest.mark.parametrize("m", [11, 16])
+def test_16_token_gemv_deterministic_and_graph_replay(m: int, device: torch.device) -> None:
+    w = cases.layer_weights(3584, 3584, 0).to(device)
+    x = cases.activations(m, 3584, 0).to(device)
+    y1 = _linear(x, w)
+    assert torch.equal(_linear(x, w), y1)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _linear(x, w)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y_graph = _linear(x, w)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, y1)

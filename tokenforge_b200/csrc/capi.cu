@@ -36,7 +36,7 @@ struct BucketEntry {
 // (config.py:8); larger buckets extend it to the prefill sizes of the benchmark configs.
 constexpr BucketEntry kTable[] = {
     {1, kKernelGemv, 8},      {2, kKernelGemv, 8},      {4, kKernelGemv, 8},
-    {8, kKernelGemv, 8},      {16, kKernelTcGemm, 16},  {32, kKernelTcGemm, 32},
+    {8, kKernelGemv, 8},      {16, kKernelGemv, 16},    {32, kKernelTcGemm, 32},
     {64, kKernelTcGemm, 64},  {128, kKernelTcGemm, 128}, {256, kKernelTcGemm, 256},
     {512, kKernelTcGemm, 256}, {1024, kKernelTcGemm, 256}, {2048, kKernelTcGemm, 256},
     {4096, kKernelTcGemm, 256}, {1 << 30, kKernelTcGemm, 256},
@@ -48,16 +48,25 @@ constexpr BucketEntry kTable[] = {
 // one block per warp. C grows further if the CTA's staged activations would exceed 100 KB of
 // shared memory; beyond clusters of 8, K is also split across clusters (fp32 partials + reduce).
 int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
-  pl->tile_m = 8;
+  pl->tile_m = M > 8 ? 16 : 8;  // 16: two 8-token MMA n-tiles per warp
   pl->tile_n = 32;
   const int64_t n_tiles = cdiv(N, 32);
   const int64_t kblocks = cdiv(K, 128);
   const int64_t target = 2 * kNumSms;
+  auto x_bytes = [&](int64_t sp) { return 2 * M * (cdiv(kblocks, sp) * 128 + 8); };
+  const int64_t x_cap = M > 8 ? 96 * 1024 : 100 * 1024;
+  // 16 tokens: the CTA search prefers K shares whose activations stay within 64 KB per CTA
+  // (measured: gate_up at M = 12 staged 86 KB per CTA and ran 37% slower than with a 2-CTA
+  // cluster); x_cap still bounds what a cluster of 8 may stage.
+  const int64_t x_soft = 64 * 1024;
   int best_wk = 1, best_c = 1;
   int64_t best_ctas = -1;
   for (int c = 1; c <= 8; c *= 2) {
     for (int wk = 1; wk <= 8; wk *= 2) {
       if (static_cast<int64_t>(wk) * c > kblocks && !(wk == 1 && c == 1)) continue;
+      // 16 tokens: count the cluster's K split toward the staged activations' cap here, so the
+      // CTA count is not doubled after the choice (M <= 8 keeps its measured plans).
+      if (M > 8 && c < 8 && x_bytes(c) > x_soft && !(wk == 1 && c == 1)) continue;
       const int64_t ctas = cdiv(n_tiles, 8 / wk) * c;
       if (ctas > target && !(wk == 1 && c == 1)) continue;
       const bool better = ctas > best_ctas ||
@@ -70,10 +79,10 @@ int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
       }
     }
   }
-  // Shared-memory bound on the staged activations: M x (K / splits) fp16 <= 100 KB.
+  // Shared-memory bound on the staged activations: M x (K / splits) fp16 <= 100 KB (96 KB for
+  // the 16-token kernel, whose reduction buffer is 16 KB), so that two CTAs fit an SM.
   int64_t splits = best_c;
-  auto x_bytes = [&](int64_t sp) { return 2 * M * (cdiv(kblocks, sp) * 128 + 8); };
-  while (x_bytes(splits) > 100 * 1024 && splits < kblocks) splits *= 2;
+  while (x_bytes(splits) > x_cap && splits < kblocks) splits *= 2;
   int cluster = static_cast<int>(std::min<int64_t>(splits, 8));
   const int64_t per = cdiv(kblocks, splits);
   splits = cdiv(kblocks, per);
@@ -82,7 +91,7 @@ int plan_gemv(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   // splitting K 16 ways: same warps, but the split is summed in shared memory instead of
   // through two cluster barriers (about 1 us per launch). Its staged activations may use most
   // of the SM's shared memory.
-  if (best_wk == 8 && cluster == 2 && splits == 2 && x_bytes(1) <= 200 * 1024) {
+  if (M <= 8 && best_wk == 8 && cluster == 2 && splits == 2 && x_bytes(1) <= 200 * 1024) {
     best_wk = 16;
     cluster = 1;
     splits = 1;
@@ -155,6 +164,10 @@ int plan_linear(int64_t M, int64_t N, int64_t K, int group_size, LinearPlan* pl)
   pl->kernel = kTable[idx].kernel;
   if (pl->kernel == kKernelTcGemm && !tc_gemm_supported(M, N, K, group_size))
     pl->kernel = kKernelMmaGemm;
+  if (pl->kernel == kKernelGemv && M > 8 && group_size != 128) {
+    // The 16-token GEMV folds one scale per 128-wide block: other group sizes take a GEMM.
+    pl->kernel = tc_gemm_supported(M, N, K, group_size) ? kKernelTcGemm : kKernelMmaGemm;
+  }
   if (pl->kernel == kKernelGemv && !gemv_fits(M, N, K, K, group_size))
     pl->kernel = kKernelMmaGemm;
   if (pl->kernel == kKernelTcGemm) {

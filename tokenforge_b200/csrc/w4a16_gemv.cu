@@ -437,6 +437,66 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
+// Stages x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory, rows xs_stride apart: every
+// 16-byte piece is an asynchronous copy, all in flight together, so staging costs one L2 round
+// trip (e4m3 codes are converted to their exact fp16 values on the way). Returns once this
+// thread's copies have landed; the caller synchronises the CTA.
+__device__ __forceinline__ void stage_activations(const GemvParams& p, uint4* xs_smem, int kb0,
+                                                  int kb1) {
+  {
+    const int vec_per_row = (kb1 - kb0) * (kKB / 8);
+    const int total = p.M * vec_per_row;
+    const int k_lo = kb0 * kKB;
+    if (p.x8 != nullptr) {
+      // e4m3 codes: 8 bytes per 16-byte fp16 vector, converted exactly (every e4m3 value is an
+      // fp16 value; NaN stays NaN). Two loads per thread are in flight before the stores.
+      for (int i0 = threadIdx.x; i0 < total; i0 += 2 * blockDim.x) {
+        uint2 raw[2];
+        int idx[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = i0 + u * static_cast<int>(blockDim.x);
+          idx[u] = i;
+          raw[u] = make_uint2(0u, 0u);
+          if (i < total) {
+            const int m = i / vec_per_row, v = i - m * vec_per_row;
+            const int k = k_lo + 8 * v;
+            if (k < p.K) raw[u] = __ldg(reinterpret_cast<const uint2*>(p.x8 + m * p.ldx + k));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = idx[u];
+          if (i >= total) continue;
+          const int m = i / vec_per_row, v = i - m * vec_per_row;
+          const uint32_t w[2] = {raw[u].x, raw[u].y};
+          uint32_t h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint16_t pair = static_cast<uint16_t>(w[e >> 1] >> (16 * (e & 1)));
+            asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h[e]) : "h"(pair));
+          }
+          xs_smem[(m * p.xs_stride) / 8 + v] = make_uint4(h[0], h[1], h[2], h[3]);
+        }
+      }
+    } else
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int m = i / vec_per_row, v = i - m * vec_per_row;
+      const int k = k_lo + 8 * v;
+      uint4* dst = xs_smem + (m * p.xs_stride) / 8 + v;
+      if (k < p.K) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                     "l"(p.x + m * p.ldx + k)
+                     : "memory");
+      } else {
+        *dst = zero4();
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  }
+}
+
 // Fused RMSNorm + FP8 prologue on the staged rows (the CTA holds all K of each of the M rows):
 // the rule of rmsnorm_fp8_quant (tf_rmsnorm.cuh) applied in shared memory. Pass 1 sums the
 // squares in fp64, pass 2 writes y = fp16(x * rstd) * weight in place and takes amax|y|, pass 3
@@ -576,60 +636,7 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   // The peer call counter is read after the wait: the previous call on this stream has ended.
   const uint32_t call = p.peer_world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.peer_ctl) : 0u;
 
-  // Stage x[0:M, kb0*128 : kb1*128] (zero past K) in shared memory: every 16-byte piece is an
-  // asynchronous copy, all in flight together, so staging costs one L2 round trip.
-  {
-    const int vec_per_row = (kb1 - L.kb0) * (kKB / 8);
-    const int total = p.M * vec_per_row;
-    const int k_lo = L.kb0 * kKB;
-    if (p.x8 != nullptr) {
-      // e4m3 codes: 8 bytes per 16-byte fp16 vector, converted exactly (every e4m3 value is an
-      // fp16 value; NaN stays NaN). Two loads per thread are in flight before the stores.
-      for (int i0 = threadIdx.x; i0 < total; i0 += 2 * blockDim.x) {
-        uint2 raw[2];
-        int idx[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int i = i0 + u * static_cast<int>(blockDim.x);
-          idx[u] = i;
-          raw[u] = make_uint2(0u, 0u);
-          if (i < total) {
-            const int m = i / vec_per_row, v = i - m * vec_per_row;
-            const int k = k_lo + 8 * v;
-            if (k < p.K) raw[u] = __ldg(reinterpret_cast<const uint2*>(p.x8 + m * p.ldx + k));
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int i = idx[u];
-          if (i >= total) continue;
-          const int m = i / vec_per_row, v = i - m * vec_per_row;
-          const uint32_t w[2] = {raw[u].x, raw[u].y};
-          uint32_t h[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint16_t pair = static_cast<uint16_t>(w[e >> 1] >> (16 * (e & 1)));
-            asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h[e]) : "h"(pair));
-          }
-          xs_smem[(m * p.xs_stride) / 8 + v] = make_uint4(h[0], h[1], h[2], h[3]);
-        }
-      }
-    } else
-    for (int i = threadIdx.x; i < total; i += blockDim.x) {
-      const int m = i / vec_per_row, v = i - m * vec_per_row;
-      const int k = k_lo + 8 * v;
-      uint4* dst = xs_smem + (m * p.xs_stride) / 8 + v;
-      if (k < p.K) {
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                         static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-                     "l"(p.x + m * p.ldx + k)
-                     : "memory");
-      } else {
-        *dst = zero4();
-      }
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  }
+  stage_activations(p, xs_smem, L.kb0, kb1);
   __syncthreads();
   if constexpr (kNorm) norm_quant_staged(p, xs_smem, red, norm_scale_sh);
 
@@ -761,6 +768,233 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   }
 }
 
+// ---------------------------------------------------------------- 16-token decode GEMV
+// M = 9..16 with group size 128: the M <= 8 kernel's weight streaming and exact (q - z) unpack,
+// with every unpacked block fed to two 8-token MMA n-tiles (tokens 0-7 and 8-15), so the unpack
+// work of a weight is shared by sixteen tokens instead of eight. The accumulators of both
+// n-tiles double the per-thread state, so this kernel runs 8-warp CTAs at two per SM with the
+// register budget that allows; the K split (warps, cluster DSMEM, cross-cluster partials) and
+// every sum order are the M <= 8 kernel's.
+__device__ __forceinline__ void gcompute_grp2(float (&a0)[2][4], float (&a1)[2][4], const GSlot& s,
+                                              int bb, const GLane& L, const uint4* xs1) {
+  const uint32_t m0 = 0x000F000Fu, m1 = 0x00F000F0u;
+  const uint32_t g0 = 0x64006400u, g1 = 0x54005400u;
+  uint32_t z0[4], z1[4];
+  {
+    const uint32_t zs = s.z >> L.nib[0];
+    const uint32_t a = lop_mask_or(zs, m0, g0), b = lop_mask_or(zs >> 4, m0, g0);
+    z0[0] = __byte_perm(a, a, 0x1010u);
+    z0[1] = __byte_perm(a, a, 0x3232u);
+    z0[2] = __byte_perm(b, b, 0x1010u);
+    z0[3] = __byte_perm(b, b, 0x3232u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
+  }
+  const uint4* xp0 = L.xs + (bb - L.kb0) * (kKB / 8);
+  const uint4* xp1 = xs1 + (bb - L.kb0) * (kKB / 8);
+  const uint32_t w[4][4] = {{s.w[0].x, s.w[0].y, s.w[0].z, s.w[0].w},
+                            {s.w[1].x, s.w[1].y, s.w[1].z, s.w[1].w},
+                            {s.w[2].x, s.w[2].y, s.w[2].z, s.w[2].w},
+                            {s.w[3].x, s.w[3].y, s.w[3].z, s.w[3].w}};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 xv0 = xp0[i], xv1 = xp1[i];
+    uint32_t pa[4], pb[4], pc[4], pd[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t h = w[j][i] >> 8;
+      pa[j] = hsub2_rn(lop_mask_or(w[j][i], m0, g0), z0[j]);
+      pb[j] = hsub2_rn(lop_mask_or(w[j][i], m1, g1), z1[j]);
+      pc[j] = hsub2_rn(lop_mask_or(h, m0, g0), z0[j]);
+      pd[j] = hsub2_rn(lop_mask_or(h, m1, g1), z1[j]);
+    }
+    const uint32_t t0a[4] = {pa[0], pa[1], pb[0], pb[1]}, t0b[4] = {pc[0], pc[1], pd[0], pd[1]};
+    const uint32_t t1a[4] = {pa[2], pa[3], pb[2], pb[3]}, t1b[4] = {pc[2], pc[3], pd[2], pd[3]};
+    if (i == 0) {
+      mma_16816_zc(a0[0], t0a, xv0.x, xv0.y);
+      mma_16816_zc(a0[1], t1a, xv0.x, xv0.y);
+      mma_16816_zc(a1[0], t0a, xv1.x, xv1.y);
+      mma_16816_zc(a1[1], t1a, xv1.x, xv1.y);
+    } else {
+      mma_16816(a0[0], t0a, xv0.x, xv0.y);
+      mma_16816(a0[1], t1a, xv0.x, xv0.y);
+      mma_16816(a1[0], t0a, xv1.x, xv1.y);
+      mma_16816(a1[1], t1a, xv1.x, xv1.y);
+    }
+    mma_16816(a0[0], t0b, xv0.z, xv0.w);
+    mma_16816(a0[1], t1b, xv0.z, xv0.w);
+    mma_16816(a1[0], t0b, xv1.z, xv1.w);
+    mma_16816(a1[1], t1b, xv1.z, xv1.w);
+  }
+}
+
+// y += s * block sum for one n-tile (accumulator per row tile; layout as fold_grp).
+__device__ __forceinline__ void fold_grp1(float (&y)[2][4], const float (&a)[2][4], const GSlot& s) {
+  const uint32_t sp[2] = {s.s.x, s.s.y};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t sh = (j & 1) ? (sp[j >> 1] >> 16) : (sp[j >> 1] & 0xFFFFu);
+    const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sh)));
+    const int t = j >> 1, e = 2 * (j & 1);
+    y[t][e] = fmaf(sf, a[t][e], y[t][e]);
+    y[t][e + 1] = fmaf(sf, a[t][e + 1], y[t][e + 1]);
+  }
+}
+
+template <int WARPS_N, int WARPS_K, bool kCluster>
+__global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, 2) w4a16_gemv16_kernel(const GemvParams p) {
+  constexpr int kWarps = WARPS_N * WARPS_K;
+  static_assert(kWarps == kCtaWarps, "CTA shape");
+  extern __shared__ uint4 xs_smem[];
+  __shared__ float red[kWarps * 2 * 8 * 32];  // per warp: two n-tiles x eight values x 32 lanes
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wn = warp / WARPS_K, wk = warp % WARPS_K;
+  const int q = lane >> 2;
+  GLane L;
+  L.c = lane & 3;
+  const int n0 = (blockIdx.x * WARPS_N + wn) * kWarpRows;
+  const int rr = n0 + 4 * q;
+  const int r0 = min(rr, p.N - 4);
+  const int nblk = (p.K + kKB - 1) / kKB;
+  L.kb0 = blockIdx.y * p.bps;
+  const int kb1 = min(nblk, L.kb0 + p.bps);
+  const int share = (kb1 - L.kb0 + WARPS_K - 1) / WARPS_K;
+  const int b0 = L.kb0 + wk * share;
+  L.b_end = min(kb1, b0 + share);
+  const int ldw = p.K / 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) L.w[j] = p.qw + (r0 + j) * ldw + 4 * L.c;
+  L.s = reinterpret_cast<const uint2*>(p.scales + r0);
+  L.z = p.qzeros + (r0 >> 3);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) L.nib[j] = 4 * awq_nibble_of((r0 + j) & 7);
+  L.xs = xs_smem + (min(q, p.M - 1) * p.xs_stride + 32 * L.c) / 8;
+  const uint4* xs1 = xs_smem + (min(q + 8, p.M - 1) * p.xs_stride + 32 * L.c) / 8;
+  const uint32_t mask = 0x000F000Fu, magic = 0x64006400u;
+
+  GSlot s0, s1;
+  gload_grp(s0, b0, p, L);
+  gload_grp(s1, b0 + 1, p, L);
+  pdl_launch_dependents();
+  pdl_wait();
+  stage_activations(p, xs_smem, L.kb0, kb1);
+  __syncthreads();
+
+  float a0[2][4], a1[2][4];
+  float y[2][2][4] = {};  // [n-tile][row tile][value]
+  for (int b = b0; b < L.b_end; b += 2) {
+    gcompute_grp2(a0, a1, s0, b, L, xs1);
+    fold_grp1(y[0], a0, s0);
+    fold_grp1(y[1], a1, s0);
+    gload_grp(s0, b + 2, p, L);
+    if (b + 1 >= L.b_end) break;
+    gcompute_grp2(a0, a1, s1, b + 1, L, xs1);
+    fold_grp1(y[0], a0, s1);
+    fold_grp1(y[1], a1, s1);
+    gload_grp(s1, b + 3, p, L);
+  }
+  // A non-finite y: the warp recomputes its range with the per-weight dequant (the M <= 8
+  // kernel's rule), each n-tile in turn.
+  bool bad = false;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) bad |= !isfinite(y[nt][t][r]);
+  if (__any_sync(0xffffffffu, bad)) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      GLane Ln = L;
+      if (nt == 1) Ln.xs = xs1;
+      float acc[2][2][4] = {};
+      for (int b = b0; b < L.b_end; ++b) {
+        gload_grp(s0, b, p, Ln);
+        gcompute(acc, s0, b, Ln, mask, magic);
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) y[nt][t][r] = acc[t][0][r] + acc[t][1][r];
+    }
+  }
+
+  // Fixed-order reductions: the WARPS_K warps (warp order), then the cluster's CTAs (rank order).
+  float* mine = red + warp * (2 * 8 * 32);
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) mine[(nt * 8 + t * 4 + r) * 32 + lane] = y[nt][t][r];
+  __syncthreads();
+  float v[2][2][4];
+  if (wk == 0) {
+    const float* base = red + (wn * WARPS_K) * (2 * 8 * 32);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float a = 0.f;
+#pragma unroll
+          for (int w = 0; w < WARPS_K; ++w)
+            a += base[w * (2 * 8 * 32) + (nt * 8 + t * 4 + r) * 32 + lane];
+          v[nt][t][r] = a;
+        }
+  }
+  bool store = wk == 0;
+  if constexpr (kCluster) {
+    __syncthreads();
+    if (wk == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) mine[(nt * 8 + t * 4 + r) * 32 + lane] = v[nt][t][r];
+    }
+    cluster_sync();
+    const uint32_t rank = cluster_rank();
+    if (rank == 0 && wk == 0) {
+      for (int cr = 1; cr < p.cluster; ++cr)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+              v[nt][t][r] += ld_cluster_f32(mine + (nt * 8 + t * 4 + r) * 32 + lane, cr);
+    }
+    cluster_sync();
+    store = store && rank == 0;
+  }
+  if (!store) return;
+
+  const int split = static_cast<int>(blockIdx.y) / p.cluster;
+  const bool direct = static_cast<int>(gridDim.y) == p.cluster;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int n = rr + 2 * t + (r >> 1);
+        const int m = 8 * nt + 2 * L.c + (r & 1);
+        if (n >= p.N || m >= p.M) continue;
+        float o = v[nt][t][r];
+        if (p.x_scale != nullptr) o *= __ldg(p.x_scale + m * p.x_scale_stride);
+        if (direct) {
+          if (p.bias) o += __half2float(__ldg(p.bias + n));
+          p.y[m * p.ldy + n] = __float2half_rn(o);
+        } else {
+          p.partial[(static_cast<int64_t>(split) * p.M + m) * p.N + n] = o;
+        }
+      }
+}
+
 // Fixed-order reduction of split-K partials: sum splits 0..S-1, add bias, cast (w4a16.py:227-232).
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial,
                                                             int split_k, int64_t M, int64_t N,
@@ -818,6 +1052,60 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
     return TF_ERR_CUDA;
   }
   return TF_OK;
+}
+
+template <int WN, int WK, bool kCluster>
+int launch_gemv16_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
+                          cudaStream_t stream, bool pdl) {
+  auto kern = w4a16_gemv16_kernel<WN, WK, kCluster>;
+  constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 8 * 32 * sizeof(float);
+  if (smem + kStaticSmem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) {
+      last_cuda_error() = static_cast<int>(e);
+      return TF_ERR_CUDA;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid_x, plan.grid_y, 1);
+  cfg.blockDim = dim3(32 * WN * WK);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (kCluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = static_cast<unsigned>(p.cluster);
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) {
+    last_cuda_error() = static_cast<int>(e);
+    return TF_ERR_CUDA;
+  }
+  return TF_OK;
+}
+
+template <bool kCluster>
+int launch_gemv16_shape(const LinearPlan& plan, const GemvParams& p, size_t smem, cudaStream_t st,
+                        bool pdl) {
+  switch (plan.warps_k) {
+    case 1: return launch_gemv16_variant<8, 1, kCluster>(plan, p, smem, st, pdl);
+    case 2: return launch_gemv16_variant<4, 2, kCluster>(plan, p, smem, st, pdl);
+    case 4: return launch_gemv16_variant<2, 4, kCluster>(plan, p, smem, st, pdl);
+    case 8: return launch_gemv16_variant<1, 8, kCluster>(plan, p, smem, st, pdl);
+    default: return TF_ERR_INVALID_ARG;
+  }
 }
 
 template <bool kCluster, bool kFact, bool kNorm = false>
@@ -891,6 +1179,14 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   // tensor-core sums; other group sizes dequantize every weight.
   const bool fact = a.group_size == kKB;
   int st;
+  if (a.M > 8) {
+    // 16-token kernel: group size 128, no peers, no fused RMSNorm (checked by the planner).
+    if (!fact || a.peers != nullptr || a.norm_w != nullptr || a.M > 16) return TF_ERR_UNSUPPORTED;
+    st = plan.cluster > 1 ? launch_gemv16_shape<true>(plan, p, smem, stream, pdl)
+                          : launch_gemv16_shape<false>(plan, p, smem, stream, pdl);
+    if (st != TF_OK || outer == 1) return st;
+    return launch_splitk_reduce(p.partial, outer, a.M, a.N, a.bias, a.y, a.ldy, stream);
+  }
   if (a.norm_w != nullptr) {
     // The fused RMSNorm needs every CTA to hold whole rows (checked by the caller).
     if (plan.cluster != 1 || plan.split_k != 1 || a.peers != nullptr) return TF_ERR_UNSUPPORTED;

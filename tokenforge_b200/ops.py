@@ -177,7 +177,9 @@ def w4a16_linear(
         m, backend=backend, on_gpu=x.is_cuda, cuda_ext_available=cuda_ext_available()  # type: ignore[arg-type]
     )
     dispatch.record(decision)
-    entry = "gemv" if decision.kernel == "cuda_gemv" else "gemm"
+    # M <= 8: the reference's _C.w4a16_gemv contract; larger M: the launch table (the 16-token
+    # GEMV up to M = 16 with group size 128, the tensor-core GEMM above).
+    entry = "gemv" if decision.kernel == "cuda_gemv" else "linear"
     return _launch_linear(entry, x2, qweight_t, scales, qzeros, bias, group_size).reshape(out_shape)
 
 
