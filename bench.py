@@ -775,7 +775,9 @@ def main() -> None:
                 "per": "step (all GEMV launches of one sweep; achieved = algorithmic bytes / summed "
                        "per-launch device time)",
                 "peak_source": f"{src} hbm_gbs",
-                "kernel": "w4a16_gemv_kernel (decode GEMV, M<=8)",
+                "kernel": ("w4a16_gemv_kernel (decode GEMV, M<=8)" if args.m <= 8 else
+                           "w4a16_gemv16_kernel (16-token decode GEMV, M 9-16)" if args.m <= 16 else
+                           "w4a16_tc_kernel (tcgen05 GEMM)"),
                 "per_layer": per_kind,
             },
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 import torch
 
+import tokenforge_b200.ops  # noqa: F401  (registers torch.ops.tokenforge)
 from oracle import oracle
 from tests.numerics import cases
 from tokenforge_b200 import pack

@@ -181,10 +181,15 @@ __global__ void __launch_bounds__(128) awq_repack_tiled_v4_kernel(const uint32_t
     }
   }
   __syncthreads();
+  // Output rows r = 8 * (rsub + 16 * (pass & 1)) + pass / 2: the four rows a warp stores at once
+  // (rsub = 4w .. 4w+3) sit in tile rows 32 (r % 8) + r / 8 that differ modulo 32, so their
+  // shared-memory reads fall in different banks (rows 32 apart share banks at a 33-word pitch).
   const int sub = threadIdx.x & 7, rsub = threadIdx.x >> 3;
-  for (int r = rsub; r < kTileRows; r += 16) {
+#pragma unroll 4
+  for (int pass = 0; pass < 16; ++pass) {
+    const int r = 8 * (rsub + 16 * (pass & 1)) + (pass >> 1);
     const int64_t orow = static_cast<int64_t>(blockIdx.x) * kTileRows + r;
-    if (orow >= cols8 * 8) break;
+    if (orow >= cols8 * 8) continue;
     const int64_t kw = kw_base + 4 * sub;
     uint32_t* dst = out + orow * out_words + kw;
     const uint32_t* srow = &tile[32 * (r & 7) + (r >> 3)][4 * sub];
