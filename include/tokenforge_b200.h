@@ -108,9 +108,11 @@ TF_API int tf_w4a16_dequant(const int32_t* qweight_t, const uint16_t* scales, co
  *
  * tf_w4a16_gemv replaces the planned extension entry `_C.w4a16_gemv(x2, qweight_t, scales,
  * qzeros, bias, group_size)` named at ops.py:86-88 (decode, M = 1..8).
- * tf_w4a16_gemm covers M >= 9 (prefill) with the sm_100a tensor-core kernel.
+ * tf_w4a16_gemm runs the sm_100a tensor-core kernel at any M (prefill).
  * tf_w4a16_linear is the per-call dispatch of the w4a16_linear op (ops.py:48-94) through the
- * fixed per-M-bucket launch table (replacing autotune.lookup, autotune.py:190-193).
+ * fixed per-M-bucket launch table (replacing autotune.lookup, autotune.py:190-193): the
+ * decode GEMV for M <= 8, the 16-token GEMV for M = 9..16 at group size 128, the tensor-core
+ * GEMM above.
  *
  * bias may be NULL. Workspace: tf_w4a16_workspace_bytes(M, N, K, group_size) bytes of device
  * memory (may be 0, then workspace may be NULL); contents need not be initialised; it must
@@ -161,10 +163,10 @@ TF_API int tf_w4a16_linear_noalloc(const uint16_t* x, int64_t M, int64_t K, int6
  * scale_stride] (scale_stride 1: the per-token fp32 scales, 0: one static scale), y as
  * tf_w4a16_linear. No reference counterpart: the reference produces e4m3 activations but has no
  * consumer for them (BASELINE config 4's block stack needs one).
- * M <= 8 (decode GEMV): the codes are staged as their exact fp16 values and y is scaled in fp32
- * before the bias, so the result is as accurate as with fp16 activations x.
- * M > 8: x16 = fp16(e4m3 * scale) (one rounding) is written to the workspace, then the regular
- * launch table runs on it. Workspace: tf_w4a16_fp8_workspace_bytes(M, N, K, group_size).
+ * Sizes the launch table serves with a GEMV (M <= 8; M <= 16 at group size 128): the codes are
+ * staged as their exact fp16 values and y is scaled in fp32 before the bias, so the result is
+ * as accurate as with fp16 activations x. Larger M: x16 = fp16(e4m3 * scale) (one rounding)
+ * is written to the workspace, then the regular launch table runs on it. Workspace: tf_w4a16_fp8_workspace_bytes(M, N, K, group_size).
  * xq must be 8-byte aligned with ldx (bytes) % 8 == 0. */
 TF_API size_t tf_w4a16_fp8_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_size);
 TF_API int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t scale_stride,

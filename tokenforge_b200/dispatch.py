@@ -8,8 +8,9 @@ Two decisions, as in the reference:
   so it is safe under CUDA-graph capture and opaque to torch.compile.
 
 Routing differs from the reference by design: every supported call runs a CUDA kernel.
-``M <= 8`` goes to the decode GEMV (``cuda_gemv``), larger ``M`` to the tensor-core GEMM
-(``cuda_gemm``). There is no Triton path, no dequant+cuBLAS path and no CPU fallback: a call
+``M <= 8`` goes to the decode GEMV (``cuda_gemv``), larger ``M`` to the kernel library's launch
+table (``cuda_gemm``: the 16-token GEMV up to ``M = 16`` at group size 128, the tensor-core
+GEMM above). There is no Triton path, no dequant+cuBLAS path and no CPU fallback: a call
 on CPU tensors, or without the kernel library, raises.
 """
 

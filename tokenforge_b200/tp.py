@@ -237,7 +237,7 @@ def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None,  #
     an all-reduce of the fp16 partials over ``group``.
 
     ``linear(x, weights, bias) -> fp16 [M, N]`` computes the local product; by default the
-    kernel library's launch table (GEMV for M <= 8, tensor-core GEMM above)."""
+    kernel library's launch table (GEMVs up to M = 16, tensor-core GEMM above)."""
     import torch.distributed as dist
 
     if linear is None:
