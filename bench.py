@@ -264,6 +264,19 @@ class DecodeSweep:
                 dist.all_reduce(self.y[name])
 
 
+def random_w4a16(n: int, k: int, gen: torch.Generator, device: torch.device):  # type: ignore[no-untyped-def]
+    """A synthetic AWQ layer (uniform int4 codes and zeros, scales in [0.002, 0.02]) repacked on
+    the GPU into the kernel layout."""
+    from tokenforge_b200.pack import W4A16Weights
+
+    qweight = torch.randint(-(2**31), 2**31 - 1, (k, n // 8), generator=gen, dtype=torch.int32,
+                            device=device)
+    qzeros = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen,
+                           dtype=torch.int32, device=device)
+    scales = (torch.rand((k // G, n), generator=gen, device=device) * 0.018 + 0.002).to(torch.float16)
+    return W4A16Weights(torch.ops.tokenforge.awq_repack(qweight), scales, qzeros, G)
+
+
 def capture(fn, device: torch.device) -> torch.cuda.CUDAGraph:  # type: ignore[no-untyped-def]
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream(device))
@@ -394,7 +407,8 @@ def run_reference(args: argparse.Namespace) -> None:
 
 
 def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], steps: int,
-                 fuse_norm: bool = True) -> dict:
+                 fuse_norm: bool = True, rank: int = 0, world: int = 1, peers=None,  # type: ignore[no-untyped-def]
+                 barrier=None) -> dict:
     """the Qwen2.5-7B-shaped quantized block stack on the sweep's 28 layers of
     weights. Per layer: rmsnorm_fp8_quant of the fp16 residual -> W4A16 qkv on the e4m3
     activations -> the v slice (512 channels) repeated 7x stands in for attention -> W4A16 o ->
@@ -408,11 +422,14 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
     gammas = [((1 + 0.1 * torch.randn((2, HIDDEN), generator=gen, device=device))
                .to(torch.float16)) for _ in sweep.layers]
     out: dict[str, object] = {
-        "metric": "Qwen2.5-7B quantized block stack tokens/s (config 4, 28 layers, TP=1)",
+        "metric": f"Qwen2.5-7B quantized block stack tokens/s (config 4, 28 layers, TP={world})",
         "unit": "tokens/s",
         "fused_norm_linear": fuse_norm,
         "per_m": {},
     }
+    if world > 1:
+        return block_tp_metric(out, gammas, device, ms, steps, fuse_norm, rank, world, peers,
+                               barrier)
     for m in ms:
         h0 = torch.randn((m, HIDDEN), generator=gen, device=device).to(torch.float16)
 
@@ -447,6 +464,91 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
             "tokens_per_s": round(m / (ms_step * 1e-3), 1),
             "ms_per_step": round(ms_step, 4),
             "output_finite": finite,
+        }
+        del g
+    return out
+
+
+def block_tp_metric(out: dict, gammas: list, device: torch.device, ms: tuple[int, ...], steps: int,  # type: ignore[type-arg]
+                    fuse_norm: bool, rank: int, world: int, peers, barrier) -> dict:  # type: ignore[no-untyped-def]
+    """The config-4 block stack over ``world`` GPUs (tensor parallel, one rank per GPU): this
+    rank's shards of every layer, synthetic like the single-GPU leg. qkv holds [q_r | k_r | v_r]
+    and gate_up [gate_r | up_r] (tp.fused_column_bounds, gate/up on 128-column groups so that
+    gate_r is down's K shard); o and down are row shards whose partials are summed through the
+    all-reduce fused into the GEMV (M <= 8, when ``peers`` is given) or NCCL. The attention
+    stand-in tiles the rank's v slice to o's K shard width. The residual stream is replicated.
+    tokens/s = M / step time (max over ranks)."""
+    import torch.distributed as dist
+
+    import tokenforge_b200.ops as ops
+    from tokenforge_b200 import tp
+
+    q_w, kv_w = HIDDEN, 512
+    qkv_pieces = tp.fused_column_bounds((q_w, kv_w, kv_w), rank, world)
+    widths = [b - a for a, b in qkv_pieces]
+    o0, o1 = tp.row_bounds(HIDDEN, G, world)[rank]
+    i0, i1 = tp.row_bounds(INTER, G, world)[rank]
+    o_k, i_r = o1 - o0, i1 - i0
+    gen = torch.Generator(device=device).manual_seed(4242 + rank)
+    layers = [{"qkv": random_w4a16(sum(widths), HIDDEN, gen, device),
+               "o": random_w4a16(HIDDEN, o_k, gen, device),
+               "gate_up": random_w4a16(2 * i_r, HIDDEN, gen, device),
+               "down": random_w4a16(HIDDEN, i_r, gen, device)} for _ in gammas]
+    reps_of = max(1, -(-o_k // max(widths[2], 1)))
+    out["tp"] = world
+    out["sharding"] = (f"qkv [q_r|k_r|v_r] widths {widths}, o K {o_k}, gate_up [gate_r|up_r] "
+                       f"2x{i_r}, down K {i_r} (rank {rank})")
+    for m in ms:
+        fused_ok = {"o": peers is not None and peers.supports(m, HIDDEN, HIDDEN, G),
+                    "down": peers is not None and peers.supports(m, HIDDEN, INTER, G)}
+        h0 = torch.randn((m, HIDDEN), generator=torch.Generator(device=device).manual_seed(9),
+                         device=device).to(torch.float16)
+
+        def norm_linear(h: torch.Tensor, gamma: torch.Tensor, wt) -> torch.Tensor:  # type: ignore[no-untyped-def]
+            if fuse_norm:
+                return torch.ops.tokenforge.rmsnorm_fp8_w4a16_linear(
+                    h, gamma, 1e-6, None, wt.qweight_t, wt.scales, wt.qzeros, None, G)
+            q, sc = torch.ops.tokenforge.rmsnorm_fp8_quant(h, gamma, 1e-6, None)
+            return torch.ops.tokenforge.w4a16_linear_fp8(q, sc, wt.qweight_t, wt.scales,
+                                                         wt.qzeros, None, G)
+
+        def row_parallel(x: torch.Tensor, wt, name: str) -> torch.Tensor:  # type: ignore[no-untyped-def]
+            if fused_ok[name]:
+                y = peers.linear(x, wt, None)
+                if y is None:
+                    raise RuntimeError(f"fused all-reduce refused {name} at M={m}")
+                return y
+            y = ops.w4a16_gemm(x, wt.qweight_t, wt.scales, wt.qzeros, G, None)
+            dist.all_reduce(y)
+            return y
+
+        def step() -> None:
+            h = h0
+            for w, gamma in zip(layers, gammas):
+                qkv = norm_linear(h, gamma[0], w["qkv"])
+                v = qkv[:, widths[0] + widths[1]:]
+                attn = v.repeat(1, reps_of)[:, :o_k].contiguous()
+                h = h + row_parallel(attn, w["o"], "o")
+                gu = norm_linear(h, gamma[1], w["gate_up"])
+                h = h + row_parallel(ops.silu_mul(gu), w["down"], "down")
+            step.out = h  # type: ignore[attr-defined]
+
+        if barrier:
+            barrier()
+        g = capture(step, device)
+        g.replay()
+        torch.cuda.synchronize(device)
+        reps = max(2, steps if m <= 64 else steps // 4)
+        t = torch.tensor([time_graph(g, reps, device, barrier) / reps], device=device,
+                         dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+        finite = bool(torch.isfinite(step.out).all())  # type: ignore[attr-defined]
+        out["per_m"][str(m)] = {  # type: ignore[index]
+            "tokens_per_s": round(m / (ms_step * 1e-3), 1),
+            "ms_per_step": round(ms_step, 4),
+            "output_finite": finite,
+            "allreduce": {k: ("fused" if v else "nccl") for k, v in fused_ok.items()},
         }
         del g
     return out
@@ -599,6 +701,8 @@ def main() -> None:
                     help="omit the AWQ repack and RMSNorm+FP8 legs (configs 1 and 2)")
     ap.add_argument("--block-ms", type=str, default="1,64,2048",
                     help="token counts M of the config-4 block-stack leg")
+    ap.add_argument("--block-tp", action="store_true",
+                    help="with --gpus N > 1: also run the config-4 block stack tensor-parallel")
     ap.add_argument("--no-fuse-norm", action="store_true",
                     help="block stack: separate RMSNorm+FP8 and linear launches")
     ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
@@ -735,9 +839,10 @@ def main() -> None:
         extra["repack"] = repack_metric(device, max(3, args.steps // 2), pk)
         extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None
-    if world == 1 and full and not args.skip_block:
+    if full and not args.skip_block and (world == 1 or args.block_tp):
         block = block_metric(sweep, device, tuple(int(v) for v in args.block_ms.split(",")),
-                             max(3, args.steps // 2), fuse_norm=not args.no_fuse_norm)
+                             max(3, args.steps // 2), fuse_norm=not args.no_fuse_norm,
+                             rank=rank, world=world, peers=peers, barrier=barrier)
     cpu = None
     if rank == 0 and world == 1 and full and not args.skip_cpu:
         cpu = cpu_baseline(args.m, min_seconds=10.0)

@@ -135,3 +135,40 @@ def test_two_gloo_ranks_reassemble_the_full_layer(world: int) -> None:
     ref = oracle.w4a16_reference(x, w.qweight_t, w.scales, w.qzeros, G, b)
     w16 = oracle.dequantize_tf(w.qweight_t, w.scales, w.qzeros, G)
     assert float((y_row.double() - ref).abs().max()) <= 2 * atol(x, w16, "cpu") + 2e-3
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_column_shards_pair_projections(world: int) -> None:
+    """gate|up split part by part and on group boundaries: rank r holds [gate_r | up_r] whose
+    dequantised rows are the full layer's, gate_r is the K range of its down shard, and the
+    ranks' pieces tile every projection; q|k|v likewise in whole words, bias included."""
+    inter, k = 1024, 256
+    w = cases.layer_weights(2 * inter, k, 5)
+    full = oracle.dequantize_tf(w.qweight_t, w.scales, w.qzeros, w.group_size)
+    seen = []
+    for rank in range(world):
+        sh = tp.shard_fused_columns(w, (inter, inter), rank, world, group_aligned=True)
+        (g0, g1), (u0, u1) = sh.pieces
+        assert (g0, g1) == tp.row_bounds(inter, w.group_size, world)[rank]
+        assert (u0 - inter, u1 - inter) == (g0, g1)
+        got = oracle.dequantize_tf(sh.weights.qweight_t, sh.weights.scales, sh.weights.qzeros,
+                                   w.group_size)
+        assert torch.equal(got, torch.cat([full[g0:g1], full[u0:u1]]))
+        seen += [(g0, g1), (u0, u1)]
+    cover = sorted(seen)
+    assert cover[0][0] == 0 and cover[-1][1] == 2 * inter
+    assert all(a[1] == b[0] for a, b in zip(cover, cover[1:]))
+
+    parts = (256, 64, 64)
+    wq = cases.layer_weights(sum(parts), k, 6)
+    bias = cases.bias(sum(parts), 6)
+    fq = oracle.dequantize_tf(wq.qweight_t, wq.scales, wq.qzeros, wq.group_size)
+    for rank in range(world):
+        sh = tp.shard_fused_columns(wq, parts, rank, world, bias)
+        rows = torch.cat([torch.arange(a, b) for a, b in sh.pieces])
+        got = oracle.dequantize_tf(sh.weights.qweight_t, sh.weights.scales, sh.weights.qzeros,
+                                   wq.group_size)
+        assert torch.equal(got, fq[rows])
+        assert sh.bias is not None and torch.equal(sh.bias, bias[rows])
+    with pytest.raises(ValueError, match="add up"):
+        tp.shard_fused_columns(wq, (256, 64), 0, world)

@@ -14,6 +14,11 @@ K per rank must be a multiple of the group size. When the group count does not d
 world size (o: 28 groups and down: 148 groups at TP = 8) the shards are uneven: the first
 ``groups % world`` ranks take one extra group. The reference has no multi-GPU code; this module
 is the partitioning its BASELINE configs 3 and 4 call for.
+
+Fused column-parallel layers (q|k|v, gate|up) are split part by part (:func:`shard_fused_columns`):
+every rank holds its slice of each projection, so a rank's gate and up columns pair up for the
+SiLU product, and with group-aligned parts its intermediate slice is exactly the K range of its
+down_proj row shard.
 """
 
 from __future__ import annotations
@@ -82,8 +87,45 @@ class LayerShard:
 
     kind: str  # "column" or "row"
     weights: W4A16Weights
-    bounds: tuple[int, int]  # columns (column-parallel) or K range (row-parallel)
+    bounds: tuple[int, int]  # columns (column-parallel; a fused layer's first piece) or K range
     bias: torch.Tensor | None
+    # Fused column-parallel layers: the global column range of each piece, in the order the
+    # pieces are concatenated in ``weights`` (one range per projection).
+    pieces: tuple[tuple[int, int], ...] = ()
+
+
+def fused_column_bounds(parts: tuple[int, ...] | list[int], rank: int, world: int,
+                        group_size: int | None = None) -> list[tuple[int, int]]:
+    """Global column ranges of ``rank``'s pieces of a layer whose output concatenates
+    projections of widths ``parts``: each projection split on its own, in whole 8-column words,
+    or in whole ``group_size``-column groups when given (so that the pieces line up with
+    :func:`row_bounds` of the next layer's K)."""
+    out, off = [], 0
+    for p in parts:
+        a, b = (row_bounds(p, group_size, world) if group_size else column_bounds(p, world))[rank]
+        out.append((off + a, off + b))
+        off += p
+    return out
+
+
+def shard_fused_columns(w: W4A16Weights, parts: tuple[int, ...] | list[int], rank: int, world: int,
+                        bias: torch.Tensor | None = None, group_aligned: bool = False) -> LayerShard:
+    """Column-parallel shard of a fused layer (q|k|v with parts (q, k, v); gate|up with parts
+    (I, I)): rank r holds its slice of every projection, concatenated in part order, so its
+    output is [q_r | k_r | v_r] or [gate_r | up_r]. ``group_aligned`` splits each projection in
+    whole quantization groups of columns (for gate|up, so that gate_r matches down's K shard)."""
+    if sum(parts) != w.n:
+        raise ValueError(f"parts {tuple(parts)} do not add up to N={w.n}")
+    pieces = fused_column_bounds(parts, rank, world, w.group_size if group_aligned else None)
+    shards = [shard_columns(w, a, b) for a, b in pieces]
+    weights = W4A16Weights(
+        torch.cat([s.qweight_t for s in shards], dim=0),
+        torch.cat([s.scales for s in shards], dim=1),
+        torch.cat([s.qzeros for s in shards], dim=1),
+        w.group_size,
+    )
+    b = None if bias is None else torch.cat([bias[a:bb] for a, bb in pieces]).contiguous()
+    return LayerShard("column", weights, pieces[0], b, tuple(pieces))
 
 
 def shard_layer(
