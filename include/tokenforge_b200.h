@@ -186,7 +186,7 @@ TF_API int tf_w4a16_linear_fp8(const uint8_t* xq, const float* x_scale, int64_t 
  * not NULL). Returns TF_ERR_UNSUPPORTED (launching nothing) for M > 8 and for layers whose
  * decode plan splits K across CTAs; the caller then makes the two calls. Workspace as
  * tf_w4a16_linear (none for the plans it accepts). Every CTA normalises all M rows itself, so
- * the fused call pays off at M = 1; on B200 two calls are faster from M = 2 on. */
+ * the fused call pays off at M <= 2; on B200 two calls are faster from M = 4 on. */
 TF_API int tf_rmsnorm_fp8_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
                     const uint16_t* norm_weight, float eps, const float* static_scale,
                     float* scale_out, const int32_t* qweight_t, const uint16_t* scales,

@@ -503,7 +503,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint4* xs
 // replaces y by the exact fp16 value of its e4m3 code e4m3(y / scale). The GEMV then runs
 // exactly as on rmsnorm_fp8_quant's (codes, scale) and multiplies y by scale[m] in fp32, so its
 // output is bit-identical to the two-kernel path. red: >= 3 * 8 * warps floats of scratch.
-__device__ __noinline__ void norm_quant_staged(const GemvParams& p, uint4* xs, float* red,
+__device__ __forceinline__ void norm_quant_staged(const GemvParams& p, uint4* xs, float* red,
                                                float* scale_sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nw = static_cast<int>(blockDim.x) >> 5, nt = static_cast<int>(blockDim.x);

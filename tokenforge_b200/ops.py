@@ -294,12 +294,13 @@ def rmsnorm_fp8_w4a16_linear(
     bias: torch.Tensor | None,
     group_size: int,
 ) -> torch.Tensor:
-    """``w4a16_linear_fp8(*rmsnorm_fp8_quant(x, norm_weight, eps, scale), ...)``. For one token
-    on a layer whose decode plan keeps K in one CTA, this is one kernel: the normalised and
-    quantised activations stay in shared memory, and y is bit-identical to the two-op path.
+    """``w4a16_linear_fp8(*rmsnorm_fp8_quant(x, norm_weight, eps, scale), ...)``. For one or two
+    tokens on a layer whose decode plan keeps K in one CTA, this is one kernel: the normalised
+    and quantised activations stay in shared memory, and y is bit-identical to the two-op path.
     Otherwise the two ops run (both on the GPU): every CTA of the fused kernel normalises all
-    M rows itself, which on B200 costs more than the saved launch from M = 2 on (measured in
-    the block stack: +2.7% tokens/s at M = 1, -21% at M = 8). No reference counterpart."""
+    M rows itself, which on B200 costs more than the saved launch from M = 4 on (measured in
+    the config-4 block stack: +10.6% tokens/s at M = 1, +3.1% at 2, -6% at 4, -17% at 8).
+    No reference counterpart."""
     k = x.shape[-1]
     n = qweight_t.shape[0]
     out_shape = (*x.shape[:-1], n)
@@ -322,7 +323,7 @@ def rmsnorm_fp8_w4a16_linear(
         if tuple(bias.shape) != (n,) or bias.dtype != torch.float16:
             raise ValueError(f"bias must be fp16 [{n}]")
         bias = bias.contiguous()
-    if m == 1:
+    if m <= 2:
         xc = x2
         if xc.stride(-1) != 1 or xc.data_ptr() % _VEC:
             xc = x2.contiguous()
