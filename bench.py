@@ -408,7 +408,7 @@ def run_reference(args: argparse.Namespace) -> None:
 
 def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], steps: int,
                  fuse_norm: bool = True, rank: int = 0, world: int = 1, peers=None,  # type: ignore[no-untyped-def]
-                 barrier=None) -> dict:
+                 barrier=None, fuse_silu: bool = True) -> dict:
     """the Qwen2.5-7B-shaped quantized block stack on the sweep's 28 layers of
     weights. Per layer: rmsnorm_fp8_quant of the fp16 residual -> W4A16 qkv on the e4m3
     activations -> the v slice (512 channels) repeated 7x stands in for attention -> W4A16 o ->
@@ -425,6 +425,7 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
         "metric": f"Qwen2.5-7B quantized block stack tokens/s (config 4, 28 layers, TP={world})",
         "unit": "tokens/s",
         "fused_norm_linear": fuse_norm,
+        "fused_silu_linear": fuse_silu and world == 1,
         "per_m": {},
     }
     if world > 1:
@@ -449,9 +450,13 @@ def block_metric(sweep: DecodeSweep, device: torch.device, ms: tuple[int, ...], 
                 v = qkv[:, 4096:].repeat(1, 7)
                 h = h + ops.w4a16_gemm(v, w["o"].qweight_t, w["o"].scales, w["o"].qzeros, G)
                 gu = norm_linear(h, gamma[1], w["gate_up"])
-                a = ops.silu_mul(gu)
-                h = h + ops.w4a16_gemm(a, w["down"].qweight_t, w["down"].scales,
-                                       w["down"].qzeros, G)
+                if fuse_silu:
+                    h = h + torch.ops.tokenforge.silu_mul_w4a16_linear(
+                        gu, w["down"].qweight_t, w["down"].scales, w["down"].qzeros, None, G)
+                else:
+                    a = ops.silu_mul(gu)
+                    h = h + ops.w4a16_gemm(a, w["down"].qweight_t, w["down"].scales,
+                                           w["down"].qzeros, G)
             step.out = h  # type: ignore[attr-defined]
 
         g = capture(step, device)
@@ -703,6 +708,8 @@ def main() -> None:
                     help="token counts M of the config-4 block-stack leg")
     ap.add_argument("--block-tp", action="store_true",
                     help="with --gpus N > 1: also run the config-4 block stack tensor-parallel")
+    ap.add_argument("--no-fuse-silu", action="store_true",
+                    help="block stack: separate SiLU-product and down-projection launches")
     ap.add_argument("--no-fuse-norm", action="store_true",
                     help="block stack: separate RMSNorm+FP8 and linear launches")
     ap.add_argument("--layer", choices=[s[0] for s in LAYER_SHAPES], action="append",
@@ -842,7 +849,8 @@ def main() -> None:
     if full and not args.skip_block and (world == 1 or args.block_tp):
         block = block_metric(sweep, device, tuple(int(v) for v in args.block_ms.split(",")),
                              max(3, args.steps // 2), fuse_norm=not args.no_fuse_norm,
-                             rank=rank, world=world, peers=peers, barrier=barrier)
+                             rank=rank, world=world, peers=peers, barrier=barrier,
+                             fuse_silu=not args.no_fuse_silu)
     cpu = None
     if rank == 0 and world == 1 and full and not args.skip_cpu:
         cpu = cpu_baseline(args.m, min_seconds=10.0)

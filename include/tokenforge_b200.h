@@ -194,6 +194,18 @@ TF_API int tf_rmsnorm_fp8_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, 
                     uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* W4A16 linear on the SiLU-gated product of a gate_up output, for decode (M <= 8):
+ *   y = w4a16_linear(silu_mul(gate_up), W) in one kernel, bit-identical to tf_silu_mul followed
+ * by tf_w4a16_linear. Each CTA computes the products of the K range it stages, so the [M, K]
+ * intermediate never goes to HBM and one launch replaces two. No reference counterpart (it
+ * serves the MLP of BASELINE config 4's block stack). gate_up: fp16 [M, 2K], 16-byte aligned,
+ * row stride ld >= 2K with ld % 8 == 0; K is W's input size. Returns TF_ERR_UNSUPPORTED
+ * (launching nothing) for M > 8 and for layers whose decode plan splits K across CTAs. */
+TF_API int tf_silu_mul_w4a16_linear(const uint16_t* gate_up, int64_t M, int64_t K, int64_t ld,
+                    const int32_t* qweight_t, const uint16_t* scales, const int32_t* qzeros,
+                    const uint16_t* bias, int64_t N, int32_t group_size, uint16_t* y, int64_t ldy,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* SiLU-gated product of a fused gate_up projection (BASELINE config 4's block stack; no
  * reference counterpart): out[m, i] = fp16(silu(g) * u), g = gate_up[m, i],
  * u = gate_up[m, I + i], silu(g) = g / (1 + exp(-g)) in fp32. gate_up fp16 [M, 2I] with row

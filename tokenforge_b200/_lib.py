@@ -72,6 +72,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _P],
     ),
     "tf_silu_mul": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _I64, _P]),
+    "tf_silu_mul_w4a16_linear": (
+        ctypes.c_int,
+        [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _SZ, _P],
+    ),
     "tf_peer_mailbox_bytes": (_SZ, [_I32, _I32, _I32]),
     "tf_peer_mailbox_alloc": (ctypes.c_int, [_SZ, _P, _P]),
     "tf_peer_mailbox_open": (ctypes.c_int, [_P, _P]),

@@ -248,6 +248,7 @@ LinearArgs make_args(const uint16_t* x, int64_t M, int64_t K, int64_t ldx, const
   a.norm_eps = 0.f;
   a.norm_static = nullptr;
   a.norm_scale_out = nullptr;
+  a.silu = 0;
   a.x = x;
   a.M = M;
   a.K = K;
@@ -558,6 +559,31 @@ int tf_rmsnorm_fp8_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t
   // One pass: every CTA must hold whole rows (no K split across CTAs).
   if (pl.kernel != kKernelGemv || !gemv_fits(M, N, K, ldx, group_size) || pl.split_k != 1 ||
       pl.cluster != 1)
+    return TF_ERR_UNSUPPORTED;
+  if (pl.workspace > 0 && (workspace == nullptr || workspace_bytes < pl.workspace))
+    return TF_ERR_WORKSPACE;
+  return launch_gemv(pl, a, static_cast<cudaStream_t>(stream));
+}
+
+int tf_silu_mul_w4a16_linear(const uint16_t* gate_up, int64_t M, int64_t K, int64_t ld,
+                             const int32_t* qweight_t, const uint16_t* scales,
+                             const int32_t* qzeros, const uint16_t* bias, int64_t N,
+                             int32_t group_size, uint16_t* y, int64_t ldy, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  using namespace tfb;
+  if (M < 0 || K < 1 || ld < 2 * K) return TF_ERR_INVALID_ARG;
+  if (M == 0) return TF_OK;
+  if (M > 8 || K % 8 != 0) return TF_ERR_UNSUPPORTED;
+  auto a = make_args(gate_up, M, K, ld, qweight_t, scales, qzeros, bias, N, group_size, y, ldy,
+                     workspace, workspace_bytes);
+  a.silu = 1;
+  int st = validate_linear(a);
+  if (st != TF_OK) return st;
+  LinearPlan pl;
+  st = plan_linear(M, N, K, group_size, &pl);
+  if (st != TF_OK) return st;
+  if (pl.kernel != kKernelGemv || !gemv_fits(M, N, K, ld, group_size) || pl.split_k != 1 ||
+      pl.cluster != 1 || M * ld >= (int64_t(1) << 31))
     return TF_ERR_UNSUPPORTED;
   if (pl.workspace > 0 && (workspace == nullptr || workspace_bytes < pl.workspace))
     return TF_ERR_WORKSPACE;

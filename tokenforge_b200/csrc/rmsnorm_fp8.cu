@@ -290,14 +290,13 @@ __global__ void silu_mul_kernel(const __half* __restrict__ gu, int64_t M, int64_
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 gf = __half22float2(g2[e]), uf = __half22float2(u2[e]);
-      o2[e] = __floats2half2_rn(gf.x / (1.0f + expf(-gf.x)) * uf.x,
-                                gf.y / (1.0f + expf(-gf.y)) * uf.y);
+      o2[e] = __floats2half2_rn(silu_mul_f32(gf.x, uf.x), silu_mul_f32(gf.y, uf.y));
     }
     *reinterpret_cast<uint4*>(o) = ov;
   } else {
     for (int e = 0; e < 8 && i0 + e < I; ++e) {
       const float gf = __half2float(g[e]), uf = __half2float(u[e]);
-      o[e] = __float2half_rn(gf / (1.0f + expf(-gf)) * uf);
+      o[e] = __float2half_rn(silu_mul_f32(gf, uf));
     }
   }
 }

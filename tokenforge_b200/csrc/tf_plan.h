@@ -60,6 +60,9 @@ struct LinearArgs {
   float norm_eps;
   const float* norm_static;
   float* norm_scale_out;
+  // Fused SiLU product (silu != 0): x is a gate_up output [M, 2K] with row stride ldx, and the
+  // GEMV consumes fp16(silu(x[:, :K]) * x[:, K:]).
+  int silu;
 };
 
 // One rank's mailbox: a 256-byte header (u32 call counter, arrival counter, error word), then

@@ -36,4 +36,10 @@ __device__ __forceinline__ float dyn_scale(float amax) {
   return fmaxf(__fdiv_rn(amax, kFp8Max), kMinScale);
 }
 
+// SiLU-gated product in fp32 (before its fp16 rounding): silu(g) * u = g / (1 + exp(-g)) * u,
+// shared by the standalone kernel and the GEMV's fused staging so both round identically.
+__device__ __forceinline__ float silu_mul_f32(float g, float u) {
+  return g / (1.0f + expf(-g)) * u;
+}
+
 }  // namespace tfb

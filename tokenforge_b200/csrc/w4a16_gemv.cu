@@ -497,6 +497,35 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint4* xs
   }
 }
 
+// Fused SiLU prologue: x is the gate_up output [M, 2K] (row stride ldx), and the staged
+// activations of the CTA's K range are fp16(silu(g) * u) with g = x[m, k], u = x[m, K + k],
+// computed as the standalone silu_mul kernel computes them (silu_mul_f32), so y is
+// bit-identical to silu_mul followed by this GEMV. Elementwise: every plan shape could use it.
+__device__ __forceinline__ void stage_silu(const GemvParams& p, uint4* xs_smem, int kb0, int kb1) {
+  const int vec_per_row = (kb1 - kb0) * (kKB / 8);
+  const int total = p.M * vec_per_row;
+  const int k_lo = kb0 * kKB;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int m = i / vec_per_row, v = i - m * vec_per_row;
+    const int k = k_lo + 8 * v;
+    uint4 out = zero4();
+    if (k < p.K) {
+      const __half* row = p.x + m * p.ldx;
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(row + k));
+      const uint4 uv = __ldg(reinterpret_cast<const uint4*>(row + p.K + k));
+      const __half2* g2 = reinterpret_cast<const __half2*>(&gv);
+      const __half2* u2 = reinterpret_cast<const __half2*>(&uv);
+      __half2* o2 = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 gf = __half22float2(g2[e]), uf = __half22float2(u2[e]);
+        o2[e] = __floats2half2_rn(silu_mul_f32(gf.x, uf.x), silu_mul_f32(gf.y, uf.y));
+      }
+    }
+    xs_smem[(m * p.xs_stride) / 8 + v] = out;
+  }
+}
+
 // Fused RMSNorm + FP8 prologue on the staged rows (the CTA holds all K of each of the M rows):
 // the rule of rmsnorm_fp8_quant (tf_rmsnorm.cuh) applied in shared memory. Pass 1 sums the
 // squares in fp64, pass 2 writes y = fp16(x * rstd) * weight in place and takes amax|y|, pass 3
@@ -583,7 +612,8 @@ __device__ __forceinline__ void norm_quant_staged(const GemvParams& p, uint4* xs
   __syncthreads();
 }
 
-template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact, bool kNorm = false>
+template <int WARPS_N, int WARPS_K, bool kCluster, bool kFact, bool kNorm = false,
+          bool kSilu = false>
 __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N * WARPS_K))
     w4a16_gemv_kernel(const GemvParams p) {
   constexpr int kWarps = WARPS_N * WARPS_K;
@@ -636,7 +666,10 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   // The peer call counter is read after the wait: the previous call on this stream has ended.
   const uint32_t call = p.peer_world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.peer_ctl) : 0u;
 
-  stage_activations(p, xs_smem, L.kb0, kb1);
+  if constexpr (kSilu)
+    stage_silu(p, xs_smem, L.kb0, kb1);
+  else
+    stage_activations(p, xs_smem, L.kb0, kb1);
   __syncthreads();
   if constexpr (kNorm) norm_quant_staged(p, xs_smem, red, norm_scale_sh);
 
@@ -1010,10 +1043,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   y[m * ldy + n] = __float2half_rn(s);
 }
 
-template <int WN, int WK, bool kCluster, bool kFact, bool kNorm = false>
+template <int WN, int WK, bool kCluster, bool kFact, bool kNorm = false, bool kSilu = false>
 int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
                         cudaStream_t stream, bool pdl) {
-  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact, kNorm>;
+  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact, kNorm, kSilu>;
   // Static (the reduction buffer, 1 KB per warp) plus dynamic shared memory above the default
   // 48 KB needs the opt-in limit raised.
   constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 4 * 32 * sizeof(float);
@@ -1108,17 +1141,17 @@ int launch_gemv16_shape(const LinearPlan& plan, const GemvParams& p, size_t smem
   }
 }
 
-template <bool kCluster, bool kFact, bool kNorm = false>
+template <bool kCluster, bool kFact, bool kNorm = false, bool kSilu = false>
 int launch_gemv_shape(const LinearPlan& plan, const GemvParams& p, size_t smem, cudaStream_t st,
                       bool pdl) {
   switch (plan.warps_k) {
-    case 1: return launch_gemv_variant<8, 1, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
-    case 2: return launch_gemv_variant<4, 2, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
-    case 4: return launch_gemv_variant<2, 4, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
-    case 8: return launch_gemv_variant<1, 8, kCluster, kFact, kNorm>(plan, p, smem, st, pdl);
+    case 1: return launch_gemv_variant<8, 1, kCluster, kFact, kNorm, kSilu>(plan, p, smem, st, pdl);
+    case 2: return launch_gemv_variant<4, 2, kCluster, kFact, kNorm, kSilu>(plan, p, smem, st, pdl);
+    case 4: return launch_gemv_variant<2, 4, kCluster, kFact, kNorm, kSilu>(plan, p, smem, st, pdl);
+    case 8: return launch_gemv_variant<1, 8, kCluster, kFact, kNorm, kSilu>(plan, p, smem, st, pdl);
     case 16:
       if constexpr (kCluster) return TF_ERR_INVALID_ARG;
-      else return launch_gemv_variant<1, 16, false, kFact, kNorm>(plan, p, smem, st, pdl);
+      else return launch_gemv_variant<1, 16, false, kFact, kNorm, kSilu>(plan, p, smem, st, pdl);
     default: return TF_ERR_INVALID_ARG;
   }
 }
@@ -1186,6 +1219,13 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
                           : launch_gemv16_shape<false>(plan, p, smem, stream, pdl);
     if (st != TF_OK || outer == 1) return st;
     return launch_splitk_reduce(p.partial, outer, a.M, a.N, a.bias, a.y, a.ldy, stream);
+  }
+  if (a.silu) {
+    // The fused SiLU product: single-pass plans (checked by the caller).
+    if (plan.cluster != 1 || plan.split_k != 1 || a.peers != nullptr || a.norm_w != nullptr)
+      return TF_ERR_UNSUPPORTED;
+    return fact ? launch_gemv_shape<false, true, false, true>(plan, p, smem, stream, pdl)
+                : launch_gemv_shape<false, false, false, true>(plan, p, smem, stream, pdl);
   }
   if (a.norm_w != nullptr) {
     // The fused RMSNorm needs every CTA to hold whole rows (checked by the caller).
