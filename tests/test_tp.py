@@ -172,3 +172,25 @@ def test_fused_column_shards_pair_projections(world: int) -> None:
         assert sh.bias is not None and torch.equal(sh.bias, bias[rows])
     with pytest.raises(ValueError, match="add up"):
         tp.shard_fused_columns(wq, (256, 64), 0, world)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_block_shards_line_up(world: int) -> None:
+    """The tensor-parallel block stack's shards at every TP size: the ranks' q/k/v and gate/up
+    pieces tile each projection, gate_r and up_r have the width of the rank's down K shard and
+    start on the same group, and o's K shards tile the hidden size in whole groups."""
+    hidden, kv, inter, g = 3584, 512, 18944, 128
+    q_cover, o_cover, gate_cover = [], [], []
+    for rank in range(world):
+        (q0, q1), (k0, k1), (v0, v1) = tp.fused_column_bounds((hidden, kv, kv), rank, world)
+        assert (q1 - q0) % 8 == 0 and (k1 - k0) % 8 == 0 and v1 > v0
+        q_cover.append((q0, q1))
+        (g0, g1), (u0, u1) = tp.fused_column_bounds((inter, inter), rank, world, g)
+        d0, d1 = tp.row_bounds(inter, g, world)[rank]
+        assert (g0, g1) == (d0, d1) and (u0 - inter, u1 - inter) == (d0, d1)
+        assert d0 % g == 0 and d1 % g == 0
+        gate_cover.append((g0, g1))
+        o_cover.append(tp.row_bounds(hidden, g, world)[rank])
+    for cover, total in ((q_cover, hidden), (gate_cover, inter), (o_cover, hidden)):
+        assert cover[0][0] == 0 and cover[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(cover, cover[1:]))
