@@ -116,3 +116,33 @@ def test_fusion_rejects_inconsistent_projections(tmp_path) -> None:  # type: ign
         fused_awq_tensors(ck, ["model.layers.0.self_attn.q_proj", "model.layers.0.self_attn.o_proj"])
     with pytest.raises(CheckpointError, match="no tensor"):
         fused_awq_tensors(ck, ["model.layers.0.mlp.missing_proj"])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_awq_shards_match_the_kernel_layout_partition(tmp_path, world: int) -> None:  # type: ignore[no-untyped-def]
+    """Slicing the AWQ-layout tensors and then repacking (what each rank's loader does) gives
+    exactly tp's shard of the repacked full layer, for every linear of a Qwen2 layer."""
+    from tokenforge_b200 import tp
+    from tokenforge_b200.checkpoint import QWEN2_LINEARS, QWEN2_TP, shard_awq
+    from tokenforge_b200.pack import W4A16Weights
+
+    write_checkpoint(tmp_path, layers=1, g=64)
+    ck = Checkpoint(tmp_path)
+    for name, (block, projs) in QWEN2_LINEARS.items():
+        pre = [f"model.layers.0.{block}.{p}" for p in projs]
+        qw, qz, sc, bias = fused_awq_tensors(ck, pre)
+        parts = tuple(int(ck.get(p + ".scales").shape[1]) for p in pre)
+        full = W4A16Weights(oracle.repack_awq_to_tf(qw), sc, qz, 64)
+        kind, aligned = QWEN2_TP[name]
+        for rank in range(world):
+            s_qw, s_qz, s_sc, s_b = shard_awq(qw, qz, sc, bias, kind, rank, world, 64,
+                                              parts if kind == "column" else None, aligned)
+            if kind == "column":
+                want = tp.shard_fused_columns(full, parts, rank, world, bias, aligned)
+            else:
+                want = tp.shard_layer(full, "row", rank, world, bias)
+            assert torch.equal(oracle.repack_awq_to_tf(s_qw), want.weights.qweight_t)
+            assert torch.equal(s_sc, want.weights.scales) and torch.equal(s_qz, want.weights.qzeros)
+            assert (s_b is None) == (want.bias is None)
+            if s_b is not None:
+                assert torch.equal(s_b, want.bias)

@@ -62,3 +62,27 @@ def test_selected_layers_and_unsupported_checkpoints(tmp_path, device: torch.dev
                                                        "w_bit": 4, "version": "GEMV"})
     with pytest.raises(CheckpointError, match="packing"):
         load_decoder_layers(tmp_path / "b", device)
+
+
+def test_tensor_parallel_load_equals_sharding_the_full_load(tmp_path, device: torch.device) -> None:  # type: ignore[no-untyped-def]
+    """load_decoder_layers(rank=r, world=2) slices before the repack; the result equals
+    tp's shards of the full load (q|k|v and gate|up projection by projection, o/down by K)."""
+    from tokenforge_b200 import tp
+
+    write_checkpoint(tmp_path, layers=1, g=128)
+    full = load_decoder_layers(tmp_path, device)[0]
+    for rank in range(2):
+        part = load_decoder_layers(tmp_path, device, rank=rank, world=2)[0]
+        want = {
+            "qkv": tp.shard_fused_columns(full.qkv, (HIDDEN, KV, KV), rank, 2, full.qkv_bias),
+            "o": tp.shard_layer(full.o, "row", rank, 2),
+            "gate_up": tp.shard_fused_columns(full.gate_up, (full.gate_up.n // 2,) * 2, rank, 2,
+                                              group_aligned=True),
+            "down": tp.shard_layer(full.down, "row", rank, 2),
+        }
+        for name, w in part.linears().items():
+            ws = want[name].weights
+            assert torch.equal(w.qweight_t, ws.qweight_t), name
+            assert torch.equal(w.scales, ws.scales) and torch.equal(w.qzeros, ws.qzeros), name
+        assert part.qkv_bias is not None and torch.equal(part.qkv_bias, want["qkv"].bias)
+        assert torch.equal(part.input_norm, full.input_norm)

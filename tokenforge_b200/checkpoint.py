@@ -20,7 +20,10 @@ ships no reader. Here:
   along N.
 * :func:`load_decoder_layers` returns each decoder layer's four linear layers as
   :class:`~tokenforge_b200.pack.W4A16Weights` (repacked once on the GPU by the bit-exact
-  ``tokenforge::awq_repack``), the q/k/v bias and the two RMSNorm weights.
+  ``tokenforge::awq_repack``), the q/k/v bias and the two RMSNorm weights. With ``world > 1``
+  it returns tensor-parallel rank ``rank``'s shards instead (:func:`shard_awq`, the partition
+  of :mod:`tokenforge_b200.tp`): the AWQ-layout tensors are sliced before the repack, so each
+  rank repacks only its own part.
 """
 
 from __future__ import annotations
@@ -231,6 +234,44 @@ def fused_awq_tensors(
     return cat(0), cat(1), cat(2), bias
 
 
+def shard_awq(
+    qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,
+    kind: str, rank: int, world: int, group_size: int, parts: tuple[int, ...] | None = None,
+    group_aligned: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """Rank ``rank``'s slice of an AWQ-layout layer (qweight [K, N/8], qzeros [K/G, N/8],
+    scales [K/G, N], bias [N]), the same partition as :mod:`tokenforge_b200.tp` applies to the
+    kernel layout: ``"column"`` takes the rank's pieces of each projection of width ``parts``
+    (the whole N when None; :func:`~tokenforge_b200.tp.fused_column_bounds`), concatenated;
+    ``"row"`` takes the rank's K range in whole groups (bias on rank 0 only)."""
+    from tokenforge_b200 import tp
+
+    n = scales.shape[1]
+    if kind == "column":
+        pieces = tp.fused_column_bounds(parts or (n,), rank, world,
+                                        group_size if group_aligned else None)
+        if sum(parts or (n,)) != n:
+            raise CheckpointError(f"parts {parts} do not add up to N={n}")
+        qw = torch.cat([qweight[:, a // 8:b // 8] for a, b in pieces], dim=1)
+        qz = torch.cat([qzeros[:, a // 8:b // 8] for a, b in pieces], dim=1)
+        sc = torch.cat([scales[:, a:b] for a, b in pieces], dim=1)
+        bs = None if bias is None else torch.cat([bias[a:b] for a, b in pieces])
+        return qw.contiguous(), qz.contiguous(), sc.contiguous(), bs
+    if kind == "row":
+        k0, k1 = tp.row_bounds(qweight.shape[0], group_size, world)[rank]
+        g0, g1 = k0 // group_size, k1 // group_size
+        bs = bias if (bias is not None and rank == 0) else None
+        return (qweight[k0:k1].contiguous(), qzeros[g0:g1].contiguous(),
+                scales[g0:g1].contiguous(), bs)
+    raise ValueError(f"kind must be 'column' or 'row', got {kind!r}")
+
+
+# How each fused linear of a Qwen2 layer shards: column-parallel projections keep every rank's
+# slice of each part (gate/up on whole groups, so gate_r is the K range of down's row shard).
+QWEN2_TP = {"qkv": ("column", False), "o": ("row", False), "gate_up": ("column", True),
+            "down": ("row", False)}
+
+
 @dataclass
 class DecoderLayer:
     """One Qwen2 decoder layer's weights in kernel layout (on the load device)."""
@@ -259,10 +300,14 @@ def num_layers(ckpt: Checkpoint, prefix: str = "model.layers.") -> int:
 
 
 def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str = "cuda",
-                        layers: list[int] | None = None,
-                        prefix: str = "model.layers.") -> list[DecoderLayer]:
+                        layers: list[int] | None = None, prefix: str = "model.layers.",
+                        rank: int = 0, world: int = 1) -> list[DecoderLayer]:
     """Each requested decoder layer (all by default) of an AWQ Qwen2 checkpoint, its linear
-    layers repacked on ``device`` (a CUDA device: the repack is a GPU kernel)."""
+    layers repacked on ``device`` (a CUDA device: the repack is a GPU kernel). With
+    ``world > 1``: tensor-parallel rank ``rank``'s shards (q|k|v and gate|up split projection by
+    projection, o and down by whole K groups; the q/k/v bias sliced with its columns)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
     ckpt = Checkpoint(path)
     cfg = AWQConfig.from_dir(ckpt.root)
     ids = list(range(num_layers(ckpt, prefix))) if layers is None else layers
@@ -281,6 +326,11 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
                 validate_awq(qw, qz, sc, cfg.group_size)
             except ValueError as e:
                 raise CheckpointError(f"{lp}{block} ({name}): {e}") from None
+            if world > 1:
+                kind, aligned = QWEN2_TP[name]
+                parts = tuple(int(ckpt.get(f"{lp}{block}.{p}.scales").shape[1]) for p in projs)
+                qw, qz, sc, bias = shard_awq(qw, qz, sc, bias, kind, rank, world, cfg.group_size,
+                                             parts if kind == "column" else None, aligned)
             ws[name] = pack_awq(qw.to(dev), qz.to(dev), sc.to(dev), cfg.group_size)
             if name == "qkv" and bias is not None:
                 qkv_bias = bias.to(device=dev, dtype=torch.float16)
@@ -298,6 +348,6 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
 
 
 __all__ = [
-    "AWQConfig", "Checkpoint", "CheckpointError", "DecoderLayer", "QWEN2_LINEARS",
-    "SafetensorsFile", "fused_awq_tensors", "load_decoder_layers", "num_layers",
+    "AWQConfig", "Checkpoint", "CheckpointError", "DecoderLayer", "QWEN2_LINEARS", "QWEN2_TP",
+    "SafetensorsFile", "fused_awq_tensors", "load_decoder_layers", "num_layers", "shard_awq",
 ]
