@@ -1,5 +1,12 @@
-// W4A16 decode GEMV for M = 1..8: y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]),
-// w = fp16(q - z) * s rounded once, fp32 accumulation, fp16 output.
+// W4A16 decode GEMVs: y[m, n] = sum_k x[m, k] * w[n, k] (+ bias[n]), w = fp16(q - z) * s
+// rounded once, fp32 accumulation, fp16 output. This file holds
+//   * w4a16_gemv_kernel, M = 1..8 (described below), with variants that take e4m3 activations
+//     (x8), fuse the row-parallel all-reduce over NVLink peer stores (peer_exchange), normalise
+//     and quantise the staged rows first (kNorm: RMSNorm + FP8), or form the SiLU products while
+//     staging (kSilu);
+//   * w4a16_gemv16_kernel, M = 9..16 at group size 128: the same weight stream feeding two
+//     8-token MMA n-tiles;
+//   * splitk_reduce_kernel for K splits that span several clusters.
 //
 // Reference semantics: tokenforge/kernels/triton/w4a16.py:44-115 (the BLOCK_M == 1 / small-M
 // paths) and its split-K contract w4a16.py:193-200,227-232 (partials summed in a fixed order,
