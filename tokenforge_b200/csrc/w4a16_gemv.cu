@@ -1050,14 +1050,13 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   y[m * ldy + n] = __float2half_rn(s);
 }
 
-template <int WN, int WK, bool kCluster, bool kFact, bool kNorm = false, bool kSilu = false>
-int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
-                        cudaStream_t stream, bool pdl) {
-  auto kern = w4a16_gemv_kernel<WN, WK, kCluster, kFact, kNorm, kSilu>;
-  // Static (the reduction buffer, 1 KB per warp) plus dynamic shared memory above the default
-  // 48 KB needs the opt-in limit raised.
-  constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 4 * 32 * sizeof(float);
-  if (smem + kStaticSmem > 48 * 1024) {
+// One launch of a GEMV kernel over the plan's grid: raises the dynamic shared-memory limit when
+// static + dynamic shared memory passes the default 48 KB, and adds the programmatic-dependent-
+// launch and cluster attributes the plan asks for.
+template <typename Kernel>
+int launch_gemv_grid(Kernel kern, const LinearPlan& plan, const GemvParams& p, size_t smem,
+                     size_t static_smem, int threads, bool cluster, cudaStream_t stream, bool pdl) {
+  if (smem + static_smem > 48 * 1024) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) {
@@ -1067,7 +1066,7 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid_x, plan.grid_y, 1);
-  cfg.blockDim = dim3(32 * WN * WK);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1077,7 +1076,7 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
-  if (kCluster) {
+  if (cluster) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
     attr[na].val.clusterDim.y = static_cast<unsigned>(p.cluster);
@@ -1094,46 +1093,21 @@ int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem
   return TF_OK;
 }
 
+template <int WN, int WK, bool kCluster, bool kFact, bool kNorm = false, bool kSilu = false>
+int launch_gemv_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
+                        cudaStream_t stream, bool pdl) {
+  // Static shared memory: the reduction buffer, 1 KB per warp.
+  constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 4 * 32 * sizeof(float);
+  return launch_gemv_grid(w4a16_gemv_kernel<WN, WK, kCluster, kFact, kNorm, kSilu>, plan, p, smem,
+                          kStaticSmem, 32 * WN * WK, kCluster, stream, pdl);
+}
+
 template <int WN, int WK, bool kCluster>
 int launch_gemv16_variant(const LinearPlan& plan, const GemvParams& p, size_t smem,
                           cudaStream_t stream, bool pdl) {
-  auto kern = w4a16_gemv16_kernel<WN, WK, kCluster>;
   constexpr size_t kStaticSmem = static_cast<size_t>(WN) * WK * 2 * 8 * 32 * sizeof(float);
-  if (smem + kStaticSmem > 48 * 1024) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) {
-      last_cuda_error() = static_cast<int>(e);
-      return TF_ERR_CUDA;
-    }
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(plan.grid_x, plan.grid_y, 1);
-  cfg.blockDim = dim3(32 * WN * WK);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  if (kCluster) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 1;
-    attr[na].val.clusterDim.y = static_cast<unsigned>(p.cluster);
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess) {
-    last_cuda_error() = static_cast<int>(e);
-    return TF_ERR_CUDA;
-  }
-  return TF_OK;
+  return launch_gemv_grid(w4a16_gemv16_kernel<WN, WK, kCluster>, plan, p, smem, kStaticSmem,
+                          32 * WN * WK, kCluster, stream, pdl);
 }
 
 template <bool kCluster>
