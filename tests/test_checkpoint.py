@@ -146,3 +146,24 @@ def test_awq_shards_match_the_kernel_layout_partition(tmp_path, world: int) -> N
             assert (s_b is None) == (want.bias is None)
             if s_b is not None:
                 assert torch.equal(s_b, want.bias)
+
+
+def test_layer_gaps_and_unquantised_linears_are_refused(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    """Errors that stop a load before anything reaches the GPU: a checkpoint whose layer ids have
+    a gap, and one that leaves a served linear unquantised (modules_to_not_convert)."""
+    from tokenforge_b200.checkpoint import load_decoder_layers
+
+    tensors = write_checkpoint(tmp_path / "gap", layers=1)
+    extra = {k.replace("layers.0.", "layers.2."): v for k, v in tensors.items()
+             if k.startswith("model.layers.0.")}
+    safetensors_torch.save_file(extra, str(tmp_path / "gap" / "extra.safetensors"))
+    with pytest.raises(CheckpointError, match="missing \\[1\\]"):
+        num_layers(Checkpoint(tmp_path / "gap"))
+
+    write_checkpoint(tmp_path / "skip", layers=1, config={
+        "zero_point": True, "q_group_size": 128, "w_bit": 4, "version": "GEMM",
+        "modules_to_not_convert": ["mlp.down_proj"]})
+    with pytest.raises(CheckpointError, match="unquantised"):
+        load_decoder_layers(tmp_path / "skip", "cpu")
+    with pytest.raises(ValueError, match="rank"):
+        load_decoder_layers(tmp_path / "skip", "cpu", rank=2, world=2)

@@ -311,6 +311,14 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
     ckpt = Checkpoint(path)
     cfg = AWQConfig.from_dir(ckpt.root)
     ids = list(range(num_layers(ckpt, prefix))) if layers is None else layers
+    # Refuse unserved checkpoints before any tensor is read or moved to the device.
+    for i in ids:
+        for block, projs in QWEN2_LINEARS.values():
+            for p in projs:
+                if any(m in f"{prefix}{i}.{block}.{p}" for m in cfg.modules_to_not_convert):
+                    raise CheckpointError(f"{prefix}{i}.{block}.{p}: left unquantised by the "
+                                          f"checkpoint (modules_to_not_convert); only AWQ "
+                                          f"linears are served")
     dev = torch.device(device)
     out = []
     for i in ids:
@@ -318,9 +326,6 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
         ws: dict[str, W4A16Weights] = {}
         qkv_bias = None
         for name, (block, projs) in QWEN2_LINEARS.items():
-            if any(m in f"{lp}{block}.{p}" for p in projs for m in cfg.modules_to_not_convert):
-                raise CheckpointError(f"{lp}{block}: left unquantised by the checkpoint "
-                                      f"(modules_to_not_convert); only AWQ linears are served")
             qw, qz, sc, bias = fused_awq_tensors(ckpt, [f"{lp}{block}.{p}" for p in projs])
             try:
                 validate_awq(qw, qz, sc, cfg.group_size)
