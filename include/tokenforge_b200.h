@@ -264,7 +264,8 @@ TF_API int tf_w4a16_linear_allreduce(const uint16_t* x, int64_t M, int64_t K, in
 /* Launch-table introspection (replaces config.default_config / GemmConfig, config.py:23-92).
  * Writes the launch chosen for (M, N, K, G) into out[0..8]:
  *   {kernel (0 = gemv, 1 = mma gemm, 2 = tcgen05 gemm), m_bucket, tile_n, warps_k, split_k,
- *    tile_m, grid_x, grid_z, cluster}. Returns TF_OK or TF_ERR_INVALID_ARG. */
+ *    tile_m, grid_x, grid_z, cluster}. A gemv with tile_m 16 is the 16-token kernel (M 9..16).
+ * Returns TF_OK or TF_ERR_INVALID_ARG. */
 TF_API int tf_launch_plan(int64_t M, int64_t N, int64_t K, int32_t group_size, int32_t* out);
 
 /* ------------------------------------------------------------------------- RMSNorm + FP8
