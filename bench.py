@@ -49,6 +49,12 @@ LAYER_SHAPES = [
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
+def _qwen7b_heads():  # type: ignore[no-untyped-def]
+    from tokenforge_b200.tp import AttentionHeads
+
+    return AttentionHeads(28, 4, 128)
+
+
 def algorithmic_bytes(m: int, n: int, k: int, g: int = G) -> int:
     return n * k // 2 + (k // g) * n * 2 + (k // g) * n // 2 + m * k * 2 + m * n * 2
 
@@ -489,9 +495,15 @@ def block_tp_metric(out: dict, gammas: list, device: torch.device, ms: tuple[int
     from tokenforge_b200 import tp
 
     q_w, kv_w = HIDDEN, 512
-    qkv_pieces = tp.fused_column_bounds((q_w, kv_w, kv_w), rank, world)
+    try:  # q|k|v and o on whole heads (28 q heads, 4 KV heads of 128): TP 1, 2 and 4
+        qkv_pieces, (o0, o1) = tp.attention_bounds(_qwen7b_heads(), rank, world, G)
+        attn_split = "heads"
+    except ValueError:  # TP 8: 28 heads do not split 8 ways; the stand-in has no real heads
+        qkv_pieces = tp.fused_column_bounds((q_w, kv_w, kv_w), rank, world)
+        o0, o1 = tp.row_bounds(HIDDEN, G, world)[rank]
+        attn_split = (f"8-column words (Qwen2.5-7B's 28 heads do not split over {world} ranks; "
+                      f"the attention stand-in tiles the rank's v slice to o's K shard)")
     widths = [b - a for a, b in qkv_pieces]
-    o0, o1 = tp.row_bounds(HIDDEN, G, world)[rank]
     i0, i1 = tp.row_bounds(INTER, G, world)[rank]
     o_k, i_r = o1 - o0, i1 - i0
     gen = torch.Generator(device=device).manual_seed(4242 + rank)
@@ -502,7 +514,7 @@ def block_tp_metric(out: dict, gammas: list, device: torch.device, ms: tuple[int
     reps_of = max(1, -(-o_k // max(widths[2], 1)))
     out["tp"] = world
     out["sharding"] = (f"qkv [q_r|k_r|v_r] widths {widths}, o K {o_k}, gate_up [gate_r|up_r] "
-                       f"2x{i_r}, down K {i_r} (rank {rank})")
+                       f"2x{i_r}, down K {i_r} (rank {rank}); attention split on {attn_split}")
     for m in ms:
         fused_ok = {"o": peers is not None and peers.supports(m, HIDDEN, HIDDEN, G),
                     "down": peers is not None and peers.supports(m, HIDDEN, INTER, G)}

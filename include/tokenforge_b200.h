@@ -147,7 +147,10 @@ TF_API int tf_w4a16_linear(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
  *   with split K) returns TF_ERR_TOO_LARGE without launching; use tf_w4a16_linear for it.
  * - The first call on each device (current device) looks the buffer up once
  *   (cudaGetSymbolAddress, which may load the library's kernels); make that first call before
- *   any stream capture.
+ *   any stream capture. The address is kept for the life of the process: after
+ *   cudaDeviceReset (or anything else that destroys and re-creates the device's primary
+ *   context) the kept address is stale, so do not call this entry point on that device again
+ *   in the same process.
  * - The buffer needs no clearing: each split writes its whole slice before it is read.
  * - One buffer per device: calls that can overlap on the device (several streams, several host
  *   threads) race on it. Issue them on one stream, or use tf_w4a16_linear with a workspace

@@ -1,6 +1,7 @@
 """Synthetic AWQ Qwen2-style checkpoints for the loader tests, written with the `safetensors`
 package (an independent writer of the format the loader reads). Shapes are a scaled-down
-Qwen2.5 decoder layer (hidden 256, q 256, k/v 64 each, intermediate 512). Like a real AWQ
+Qwen2.5 decoder layer (hidden 256, q 256 = 4 heads of 64, k/v 64 each = one KV head,
+intermediate 512), with a model config.json giving the head counts. Like a real AWQ
 checkpoint, each projection is real-valued weights (randn * 0.02) quantised min-max per group by
 the oracle's restatement of the reference's awq_quantize, in the AWQ 'gemm' packing."""
 
@@ -14,6 +15,7 @@ import torch
 from oracle import oracle
 
 HIDDEN, KV, INTER = 256, 64, 512
+HEADS, KV_HEADS, HEAD_DIM = 4, 1, 64  # q 4 x 64 = HIDDEN, k and v 1 x 64 = KV
 PROJS = {  # name -> (K, N)
     "self_attn.q_proj": (HIDDEN, HIDDEN),
     "self_attn.k_proj": (HIDDEN, KV),
@@ -71,4 +73,8 @@ def write_checkpoint(root: Path, layers: int = 2, g: int = 128, seed: int = 0, s
     cfg = config if config is not None else {
         "zero_point": True, "q_group_size": g, "w_bit": 4, "version": "GEMM"}
     (root / "quant_config.json").write_text(json.dumps(cfg))
+    (root / "config.json").write_text(json.dumps({
+        "architectures": ["Qwen2ForCausalLM"], "hidden_size": HIDDEN, "intermediate_size": INTER,
+        "num_attention_heads": HEADS, "num_key_value_heads": KV_HEADS,
+        "num_hidden_layers": layers}))
     return tensors

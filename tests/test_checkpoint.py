@@ -167,3 +167,54 @@ def test_layer_gaps_and_unquantised_linears_are_refused(tmp_path) -> None:  # ty
         load_decoder_layers(tmp_path / "skip", "cpu")
     with pytest.raises(ValueError, match="rank"):
         load_decoder_layers(tmp_path / "skip", "cpu", rank=2, world=2)
+
+
+def test_tensor_parallel_load_refuses_worlds_the_heads_do_not_split(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    """Attention splits on whole heads: 4 q heads do not split over 3 ranks, one q head of 64
+    columns is not a whole group of 128 at world 4, and a checkpoint without the model config
+    has no head counts. All are refused before any tensor reaches a device."""
+    import json
+
+    from tokenforge_b200.checkpoint import load_decoder_layers
+
+    write_checkpoint(tmp_path / "a", layers=1, g=128)
+    with pytest.raises(CheckpointError, match="attention heads do not split"):
+        load_decoder_layers(tmp_path / "a", "cpu", rank=0, world=3)
+    with pytest.raises(CheckpointError, match="whole groups"):
+        load_decoder_layers(tmp_path / "a", "cpu", rank=0, world=4)
+    (tmp_path / "a" / "config.json").unlink()
+    with pytest.raises(CheckpointError, match="head counts"):
+        load_decoder_layers(tmp_path / "a", "cpu", rank=0, world=2)
+    write_checkpoint(tmp_path / "b", layers=1, g=64)
+    cfg = json.loads((tmp_path / "b" / "config.json").read_text())
+    assert cfg["num_attention_heads"] * 64 == cfg["hidden_size"]
+
+
+def test_head_shards_in_awq_layout_match_the_kernel_layout(tmp_path) -> None:  # type: ignore[no-untyped-def]
+    """Slicing q|k|v and o on heads in AWQ layout and then repacking (what each rank's loader
+    does) gives exactly tp.shard_attention of the repacked full layers."""
+    from tests.awq_checkpoint import HEAD_DIM, HEADS, KV_HEADS
+    from tokenforge_b200 import tp
+    from tokenforge_b200.checkpoint import slice_awq_columns, slice_awq_rows
+    from tokenforge_b200.pack import W4A16Weights
+
+    write_checkpoint(tmp_path, layers=1, g=64)
+    ck = Checkpoint(tmp_path)
+    heads = tp.AttentionHeads(HEADS, KV_HEADS, HEAD_DIM)
+    qw, qz, sc, bias = fused_awq_tensors(
+        ck, [f"model.layers.0.self_attn.{p}" for p in ("q_proj", "k_proj", "v_proj")])
+    ow, oz, osc, _ = fused_awq_tensors(ck, ["model.layers.0.self_attn.o_proj"])
+    full_qkv = W4A16Weights(oracle.repack_awq_to_tf(qw), sc, qz, 64)
+    full_o = W4A16Weights(oracle.repack_awq_to_tf(ow), osc, oz, 64)
+    for world in (2, 4):
+        for rank in range(world):
+            want_qkv, want_o = tp.shard_attention(full_qkv, full_o, heads, rank, world, bias)
+            pieces, (k0, k1) = tp.attention_bounds(heads, rank, world, 64)
+            s_qw, s_qz, s_sc, s_b = slice_awq_columns(qw, qz, sc, bias, pieces)
+            assert torch.equal(oracle.repack_awq_to_tf(s_qw), want_qkv.weights.qweight_t)
+            assert torch.equal(s_sc, want_qkv.weights.scales)
+            assert torch.equal(s_qz, want_qkv.weights.qzeros)
+            assert s_b is not None and torch.equal(s_b, want_qkv.bias)
+            r_qw, r_qz, r_sc, _ = slice_awq_rows(ow, oz, osc, None, k0, k1, 64, rank == 0)
+            assert torch.equal(oracle.repack_awq_to_tf(r_qw), want_o.weights.qweight_t)
+            assert torch.equal(r_sc, want_o.weights.scales) and torch.equal(r_qz, want_o.weights.qzeros)

@@ -10,7 +10,7 @@ from hypothesis import strategies as st
 
 from tokenforge_b200 import dispatch
 from tokenforge_b200.config import M_BUCKETS, m_bucket
-from tokenforge_b200.metrics import FALLBACKS, KERNEL_CALLS, LabeledCounter
+from tokenforge_b200.metrics import FALLBACKS, KERNEL_CALLS, CounterMetric
 
 
 @given(st.integers(1, 4096))
@@ -83,12 +83,23 @@ def test_record_counts_calls_and_fallbacks() -> None:
 
 
 def test_counter_rejects_wrong_labels() -> None:
-    c = LabeledCounter("tf_test_counter_x", "doc", ("a",))
-    with pytest.raises(ValueError, match="expects labels"):
+    c = CounterMetric("tf_test_counter_x", "doc", ("a",))
+    with pytest.raises(ValueError, match="takes labels"):
         c.inc(b="1")
+    with pytest.raises(ValueError, match="only increases"):
+        c.inc(a="1", amount=-1.0)
     c.inc(a="1", amount=2.0)
     assert c.value(a="1") == 2.0
     assert c.snapshot() == {("1",): 2.0}
+
+
+def test_counters_export_through_prometheus() -> None:
+    prometheus_client = pytest.importorskip("prometheus_client")
+    KERNEL_CALLS.inc(kernel="cuda_gemv", bucket="1")
+    KERNEL_CALLS.inc(kernel="cuda_gemv", bucket="1")
+    text = prometheus_client.generate_latest().decode()
+    assert 'tokenforge_kernel_calls_total{bucket="1",kernel="cuda_gemv"} 2.0' in text
+    assert "# TYPE tokenforge_fallback_total counter" in text or "tokenforge_fallback" in text
 
 
 def test_backend_from_env(monkeypatch: pytest.MonkeyPatch) -> None:
@@ -98,6 +109,9 @@ def test_backend_from_env(monkeypatch: pytest.MonkeyPatch) -> None:
     assert dispatch.backend_from_env() == "marlin"
     monkeypatch.setenv(dispatch.BACKEND_ENV, "cublas")
     with pytest.raises(ValueError, match="TOKENFORGE_BACKEND"):
+        dispatch.backend_from_env()
+    monkeypatch.setenv(dispatch.BACKEND_ENV, "triton")
+    with pytest.raises(ValueError, match="no Triton path"):
         dispatch.backend_from_env()
 
 

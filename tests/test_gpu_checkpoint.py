@@ -10,7 +10,7 @@ import torch
 
 import tokenforge_b200.ops  # noqa: F401  (registers torch.ops.tokenforge)
 from oracle import oracle
-from tests.awq_checkpoint import HIDDEN, KV, write_checkpoint
+from tests.awq_checkpoint import HEAD_DIM, HEADS, HIDDEN, KV, KV_HEADS, write_checkpoint
 from tests.numerics.tolerance import atol
 from tokenforge_b200.checkpoint import CheckpointError, load_decoder_layers
 
@@ -64,21 +64,28 @@ def test_selected_layers_and_unsupported_checkpoints(tmp_path, device: torch.dev
         load_decoder_layers(tmp_path / "b", device)
 
 
-def test_tensor_parallel_load_equals_sharding_the_full_load(tmp_path, device: torch.device) -> None:  # type: ignore[no-untyped-def]
-    """load_decoder_layers(rank=r, world=2) slices before the repack; the result equals
-    tp's shards of the full load (q|k|v and gate|up projection by projection, o/down by K)."""
+@pytest.mark.parametrize(("g", "world"), [(128, 2), (64, 2), (64, 4)])
+def test_tensor_parallel_load_equals_sharding_the_full_load(tmp_path, g: int, world: int,  # type: ignore[no-untyped-def]
+                                                            device: torch.device) -> None:
+    """load_decoder_layers(rank=r, world=w) slices before the repack; the result equals tp's
+    shards of the full load: q|k|v and o on whole heads (the one KV head replicated), gate|up
+    projection by projection, down by K. Each rank's q width is its o shard's K."""
     from tokenforge_b200 import tp
 
-    write_checkpoint(tmp_path, layers=1, g=128)
+    write_checkpoint(tmp_path, layers=1, g=g)
     full = load_decoder_layers(tmp_path, device)[0]
-    for rank in range(2):
-        part = load_decoder_layers(tmp_path, device, rank=rank, world=2)[0]
+    heads = tp.AttentionHeads(HEADS, KV_HEADS, HEAD_DIM)
+    for rank in range(world):
+        part = load_decoder_layers(tmp_path, device, rank=rank, world=world)[0]
+        qkv_s, o_s = tp.shard_attention(full.qkv, full.o, heads, rank, world, full.qkv_bias)
+        q_piece = qkv_s.pieces[0]
+        assert q_piece[1] - q_piece[0] == part.o.k
         want = {
-            "qkv": tp.shard_fused_columns(full.qkv, (HIDDEN, KV, KV), rank, 2, full.qkv_bias),
-            "o": tp.shard_layer(full.o, "row", rank, 2),
-            "gate_up": tp.shard_fused_columns(full.gate_up, (full.gate_up.n // 2,) * 2, rank, 2,
-                                              group_aligned=True),
-            "down": tp.shard_layer(full.down, "row", rank, 2),
+            "qkv": qkv_s,
+            "o": o_s,
+            "gate_up": tp.shard_fused_columns(full.gate_up, (full.gate_up.n // 2,) * 2, rank,
+                                              world, group_aligned=True),
+            "down": tp.shard_layer(full.down, "row", rank, world),
         }
         for name, w in part.linears().items():
             ws = want[name].weights

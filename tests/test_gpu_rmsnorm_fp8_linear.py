@@ -162,3 +162,17 @@ def test_entry_point_rejects_bad_arguments(device: torch.device) -> None:
     bad[13] = 96  # group size
     assert lib.tf_rmsnorm_fp8_w4a16_linear(*bad) == _lib.TF_ERR_INVALID_ARG
     assert lib.tf_rmsnorm_fp8_w4a16_linear(*args) == _lib.TF_OK
+
+
+@pytest.mark.parametrize("m", [1, 2])
+def test_row_strided_view_keeps_its_stride(m: int, device: torch.device) -> None:
+    """x a slice of a wider buffer (row stride > K): the fused path must read row m at
+    x + m * stride(0), as the two-op path does."""
+    n, k = 1152, 896
+    w = cases.layer_weights(n, k, 5).to(device)
+    x, gamma = _inputs(m, k, 77, device)
+    wide = torch.full((m, k + 64), 1000.0, dtype=torch.float16, device=device)
+    wide[:, :k] = x
+    view = wide[:, :k]
+    assert view.stride(0) == k + 64
+    assert torch.equal(_fused(view, gamma, None, w, None), _two_op(x, gamma, None, w, None))

@@ -225,9 +225,12 @@ def test_dispatch_counts_buckets(device: torch.device) -> None:
     KERNEL_CALLS.reset()
     w = cases.layer_weights(128, 256, 0).to(device)
     _linear(cases.activations(3, 256, 0).to(device), w)
-    _linear(cases.activations(300, 256, 0).to(device), w, backend="triton")
+    x300 = cases.activations(300, 256, 0)
+    y300 = _linear(x300.to(device), w, backend="triton")
     assert KERNEL_CALLS.value(kernel="cuda_gemv", bucket="4") == 1
     assert KERNEL_CALLS.value(kernel="cuda_gemm", bucket="512") == 1
+    # The values of the M > 128 route, as the reference checks them (test_w4a16.py:99-105).
+    _check(y300, x300, cases.layer_weights(128, 256, 0))
 
 
 def test_drop_in_extension_module(device: torch.device) -> None:

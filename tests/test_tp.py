@@ -194,3 +194,62 @@ def test_block_shards_line_up(world: int) -> None:
     for cover, total in ((q_cover, hidden), (gate_cover, inter), (o_cover, hidden)):
         assert cover[0][0] == 0 and cover[-1][1] == total
         assert all(a[1] == b[0] for a, b in zip(cover, cover[1:]))
+
+
+QWEN7B_HEADS = tp.AttentionHeads(28, 4, 128)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_attention_shards_follow_heads(world: int) -> None:
+    """Qwen2.5-7B attention at every TP size its heads allow: each rank's q piece is whole heads,
+    its width is the rank's o_proj K shard (whole groups), the KV pieces are the KV heads its q
+    heads read, and the ranks' q pieces and o K ranges tile the hidden size."""
+    h, kv, hd = 28, 4, 128
+    q_cover, o_cover = [], []
+    for rank in range(world):
+        pieces, (k0, k1) = tp.attention_bounds(QWEN7B_HEADS, rank, world, 128)
+        (q0, q1), (a0, a1), (b0, b1) = pieces
+        assert (q0, q1) == (k0, k1), "q_r must be exactly o's K shard"
+        assert q0 % hd == 0 and q1 % hd == 0 and (q1 - q0) % 128 == 0
+        assert (a1 - a0) == (b1 - b0) and (a1 - a0) % hd == 0
+        assert h * hd <= a0 and a1 <= h * hd + kv * hd and b0 - a0 == kv * hd
+        first_kv = (a0 - h * hd) // hd
+        for head in range(q0 // hd, q1 // hd):  # every q head reads a KV head the rank holds
+            assert first_kv <= head // (h // kv) < first_kv + (a1 - a0) // hd
+        q_cover.append((q0, q1))
+        o_cover.append((k0, k1))
+    for cover in (q_cover, o_cover):
+        assert cover[0][0] == 0 and cover[-1][1] == h * hd
+        assert all(a[1] == b[0] for a, b in zip(cover, cover[1:]))
+
+
+def test_attention_shards_replicate_kv_heads_and_refuse_uneven_worlds() -> None:
+    small = tp.AttentionHeads(8, 2, 64)
+    kv_of = [tp.attention_bounds(small, r, 4)[0][1] for r in range(4)]
+    assert kv_of[0] == kv_of[1] != kv_of[2] == kv_of[3]  # each KV head on two ranks
+    with pytest.raises(ValueError, match="attention heads do not split"):
+        tp.attention_bounds(QWEN7B_HEADS, 0, 8)  # 28 heads over 8 ranks
+    with pytest.raises(ValueError, match="replicate"):
+        tp.attention_bounds(tp.AttentionHeads(28, 4, 128), 0, 14)  # 14 ranks over 4 KV heads
+    with pytest.raises(ValueError, match="whole groups"):
+        tp.attention_bounds(tp.AttentionHeads(4, 1, 64), 0, 4, 128)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_shard_attention_holds_the_head_slices(world: int) -> None:
+    heads = tp.AttentionHeads(8, 2, 32)
+    q, kvw = 8 * 32, 2 * 32
+    gen = torch.Generator().manual_seed(world)
+    qkv = cases.layer_weights(q + 2 * kvw, 256, world, 64)
+    o = cases.layer_weights(256, q, world, 64)
+    bias = torch.randn(q + 2 * kvw, generator=gen).half()
+    fq = oracle.dequantize_tf(qkv.qweight_t, qkv.scales, qkv.qzeros, 64)
+    for rank in range(world):
+        s_qkv, s_o = tp.shard_attention(qkv, o, heads, rank, world, bias)
+        cols = torch.cat([torch.arange(a, b) for a, b in s_qkv.pieces])
+        got = oracle.dequantize_tf(s_qkv.weights.qweight_t, s_qkv.weights.scales,
+                                   s_qkv.weights.qzeros, 64)
+        assert torch.equal(got, fq[cols])
+        assert s_qkv.bias is not None and torch.equal(s_qkv.bias, bias[cols])
+        assert s_o.weights.k == s_qkv.pieces[0][1] - s_qkv.pieces[0][0]
+        assert s_o.bounds == s_qkv.pieces[0]

@@ -3,8 +3,8 @@ in the library's fixed device buffer instead of a caller workspace.
 
 Called through the C ABI. Each shape runs twice in a row through the fixed-scratch entry point
 and is compared with tf_w4a16_linear given a torch-allocated workspace; both follow the same
-launch plan, so the outputs must agree within the W4A16 test tolerance (they are expected to be
-bit-identical). Shapes cover the decode GEMV with and without a cross-cluster split, the 64-token
+launch plan and the same fixed-order split-K sums, so the outputs must be bit-identical (and
+therefore also within the W4A16 test tolerance, which is checked as well). Shapes cover the decode GEMV with and without a cross-cluster split, the 64-token
 MMA kernel with split K, and the tensor-core GEMM with split K. This file is named to be
 collected last, so it also runs after the rest of the GPU suite has used the library.
 """
@@ -82,6 +82,7 @@ def test_noalloc_matches_workspace_entry(shape, with_bias: bool, device: torch.d
         assert not torch.isnan(y).any(), f"call {call}: output not fully written"
         err = float((y.float() - ref.float()).abs().max())
         assert err <= tol, f"call {call}: max abs diff {err:.3e} > tol {tol:.3e}"
+        assert torch.equal(y, ref), f"call {call}: not bit-identical to the workspace entry"
 
 
 def test_noalloc_leaves_device_memory_alone(device: torch.device) -> None:

@@ -6,6 +6,10 @@ group_size)`` for decode-sized M when ``TOKENFORGE_BACKEND=cuda`` (tokenforge/ke
 this module loads the sm_100a kernel library (and raises ImportError if it is not built), so
 the reference's availability probe behaves correctly when this module is installed under that
 name.
+
+It imports only the direct launchers (``tokenforge_b200.linear``), never
+``tokenforge_b200.ops``: the reference keeps its own ``torch.ops.tokenforge.*`` registrations
+(their Triton, torch-reference and fake paths) and only its ``cuda_gemv`` route lands here.
 """
 
 from __future__ import annotations
@@ -13,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from tokenforge_b200 import _lib
-from tokenforge_b200.ops import w4a16_gemv as _gemv
+from tokenforge_b200.linear import w4a16_gemv as _gemv
 
 _lib.lib()  # ImportError here is the "extension unavailable" signal
 

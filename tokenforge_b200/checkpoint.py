@@ -234,6 +234,31 @@ def fused_awq_tensors(
     return cat(0), cat(1), cat(2), bias
 
 
+def slice_awq_columns(
+    qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,
+    pieces: list[tuple[int, int]],
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """The global column ranges ``pieces`` (multiples of 8) of an AWQ-layout layer,
+    concatenated in order."""
+    qw = torch.cat([qweight[:, a // 8:b // 8] for a, b in pieces], dim=1)
+    qz = torch.cat([qzeros[:, a // 8:b // 8] for a, b in pieces], dim=1)
+    sc = torch.cat([scales[:, a:b] for a, b in pieces], dim=1)
+    bs = None if bias is None else torch.cat([bias[a:b] for a, b in pieces])
+    return qw.contiguous(), qz.contiguous(), sc.contiguous(), bs
+
+
+def slice_awq_rows(
+    qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,
+    k0: int, k1: int, group_size: int, keep_bias: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """K range [k0, k1) (whole groups) of an AWQ-layout layer; the bias only where kept."""
+    if k0 % group_size or k1 % group_size:
+        raise CheckpointError(f"K range [{k0}, {k1}) is not whole groups of {group_size}")
+    g0, g1 = k0 // group_size, k1 // group_size
+    return (qweight[k0:k1].contiguous(), qzeros[g0:g1].contiguous(), scales[g0:g1].contiguous(),
+            bias if keep_bias else None)
+
+
 def shard_awq(
     qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, bias: torch.Tensor | None,
     kind: str, rank: int, world: int, group_size: int, parts: tuple[int, ...] | None = None,
@@ -243,31 +268,47 @@ def shard_awq(
     scales [K/G, N], bias [N]), the same partition as :mod:`tokenforge_b200.tp` applies to the
     kernel layout: ``"column"`` takes the rank's pieces of each projection of width ``parts``
     (the whole N when None; :func:`~tokenforge_b200.tp.fused_column_bounds`), concatenated;
-    ``"row"`` takes the rank's K range in whole groups (bias on rank 0 only)."""
+    ``"row"`` takes the rank's K range in whole groups (bias on rank 0 only). Attention layers
+    of a real model are split on heads instead (:func:`load_decoder_layers`)."""
     from tokenforge_b200 import tp
 
     n = scales.shape[1]
     if kind == "column":
-        pieces = tp.fused_column_bounds(parts or (n,), rank, world,
-                                        group_size if group_aligned else None)
         if sum(parts or (n,)) != n:
             raise CheckpointError(f"parts {parts} do not add up to N={n}")
-        qw = torch.cat([qweight[:, a // 8:b // 8] for a, b in pieces], dim=1)
-        qz = torch.cat([qzeros[:, a // 8:b // 8] for a, b in pieces], dim=1)
-        sc = torch.cat([scales[:, a:b] for a, b in pieces], dim=1)
-        bs = None if bias is None else torch.cat([bias[a:b] for a, b in pieces])
-        return qw.contiguous(), qz.contiguous(), sc.contiguous(), bs
+        pieces = tp.fused_column_bounds(parts or (n,), rank, world,
+                                        group_size if group_aligned else None)
+        return slice_awq_columns(qweight, qzeros, scales, bias, pieces)
     if kind == "row":
         k0, k1 = tp.row_bounds(qweight.shape[0], group_size, world)[rank]
-        g0, g1 = k0 // group_size, k1 // group_size
-        bs = bias if (bias is not None and rank == 0) else None
-        return (qweight[k0:k1].contiguous(), qzeros[g0:g1].contiguous(),
-                scales[g0:g1].contiguous(), bs)
+        return slice_awq_rows(qweight, qzeros, scales, bias, k0, k1, group_size, rank == 0)
     raise ValueError(f"kind must be 'column' or 'row', got {kind!r}")
 
 
-# How each fused linear of a Qwen2 layer shards: column-parallel projections keep every rank's
-# slice of each part (gate/up on whole groups, so gate_r is the K range of down's row shard).
+def attention_heads(root: str | os.PathLike[str]):  # type: ignore[no-untyped-def]
+    """The model's attention head layout from its ``config.json`` (``num_attention_heads``,
+    ``num_key_value_heads`` (default: as many as the q heads), ``head_dim`` (default:
+    ``hidden_size / num_attention_heads``))."""
+    from tokenforge_b200.tp import AttentionHeads
+
+    path = Path(root) / "config.json"
+    if not path.exists():
+        raise CheckpointError(f"{root}: no config.json; a tensor-parallel load splits attention "
+                              f"on heads and needs the model's head counts")
+    cfg = json.loads(path.read_text())
+    try:
+        h = int(cfg["num_attention_heads"])
+        kv = int(cfg.get("num_key_value_heads", h))
+        hd = int(cfg.get("head_dim") or int(cfg["hidden_size"]) // h)
+    except (KeyError, TypeError, ValueError) as e:
+        raise CheckpointError(f"{path}: cannot read the attention head layout ({e})") from None
+    return AttentionHeads(h, kv, hd)
+
+
+# How the MLP's fused linears of a Qwen2 layer shard: column-parallel projections keep every
+# rank's slice of each part (gate/up on whole groups, so gate_r is the K range of down's row
+# shard). q|k|v and o split on attention heads (load_decoder_layers); their entries here are the
+# head-agnostic split of shard_awq.
 QWEN2_TP = {"qkv": ("column", False), "o": ("row", False), "gate_up": ("column", True),
             "down": ("row", False)}
 
@@ -304,13 +345,26 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
                         rank: int = 0, world: int = 1) -> list[DecoderLayer]:
     """Each requested decoder layer (all by default) of an AWQ Qwen2 checkpoint, its linear
     layers repacked on ``device`` (a CUDA device: the repack is a GPU kernel). With
-    ``world > 1``: tensor-parallel rank ``rank``'s shards (q|k|v and gate|up split projection by
-    projection, o and down by whole K groups; the q/k/v bias sliced with its columns)."""
+    ``world > 1``: tensor-parallel rank ``rank``'s shards. q|k|v and o split on whole attention
+    heads (:func:`tokenforge_b200.tp.attention_bounds`, head counts from ``config.json``): the
+    rank's q heads, their KV heads (replicated when there are more ranks than KV heads) and o's
+    K range over the same q heads, so the rank's attention output feeds its own o shard; a
+    world size the heads do not divide is refused. gate|up split projection by projection in
+    whole groups and down by the matching K groups. The q/k/v bias is sliced with its columns."""
     if not 0 <= rank < world:
         raise ValueError(f"rank {rank} outside world {world}")
     ckpt = Checkpoint(path)
     cfg = AWQConfig.from_dir(ckpt.root)
     ids = list(range(num_layers(ckpt, prefix))) if layers is None else layers
+    attn = None
+    if world > 1:
+        from tokenforge_b200 import tp
+
+        heads = attention_heads(ckpt.root)
+        try:
+            attn = tp.attention_bounds(heads, rank, world, cfg.group_size)
+        except ValueError as e:
+            raise CheckpointError(f"tensor parallel over {world} ranks: {e}") from None
     # Refuse unserved checkpoints before any tensor is read or moved to the device.
     for i in ids:
         for block, projs in QWEN2_LINEARS.values():
@@ -331,7 +385,20 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
                 validate_awq(qw, qz, sc, cfg.group_size)
             except ValueError as e:
                 raise CheckpointError(f"{lp}{block} ({name}): {e}") from None
-            if world > 1:
+            if world > 1 and name == "qkv":
+                pieces, _ = attn  # type: ignore[misc]
+                if sc.shape[1] != sum(heads.parts):
+                    raise CheckpointError(f"{lp}{block}: q|k|v N={sc.shape[1]} does not match "
+                                          f"the head layout {heads}")
+                qw, qz, sc, bias = slice_awq_columns(qw, qz, sc, bias, pieces)
+            elif world > 1 and name == "o":
+                _, (k0, k1) = attn  # type: ignore[misc]
+                if qw.shape[0] != heads.parts[0]:
+                    raise CheckpointError(f"{lp}{block}: o_proj K={qw.shape[0]} does not match "
+                                          f"the head layout {heads}")
+                qw, qz, sc, bias = slice_awq_rows(qw, qz, sc, bias, k0, k1, cfg.group_size,
+                                                  rank == 0)
+            elif world > 1:
                 kind, aligned = QWEN2_TP[name]
                 parts = tuple(int(ckpt.get(f"{lp}{block}.{p}.scales").shape[1]) for p in projs)
                 qw, qz, sc, bias = shard_awq(qw, qz, sc, bias, kind, rank, world, cfg.group_size,
@@ -354,5 +421,6 @@ def load_decoder_layers(path: str | os.PathLike[str], device: torch.device | str
 
 __all__ = [
     "AWQConfig", "Checkpoint", "CheckpointError", "DecoderLayer", "QWEN2_LINEARS", "QWEN2_TP",
-    "SafetensorsFile", "fused_awq_tensors", "load_decoder_layers", "num_layers", "shard_awq",
+    "SafetensorsFile", "attention_heads", "fused_awq_tensors", "load_decoder_layers",
+    "num_layers", "shard_awq", "slice_awq_columns", "slice_awq_rows",
 ]

@@ -41,7 +41,17 @@ MIN_SM: Final = 100  # the kernels are built for sm_100a only
 
 
 def backend_from_env() -> Backend:
+    """The layer-level backend a process asks for. ``triton`` is refused: this package carries
+    no Triton kernels, so a process that asked for them would otherwise get CUDA without being
+    told. (The op-level ``backend`` argument still accepts ``"triton"``, as the reference's op
+    schema does, and serves it with the CUDA kernels: that string names a route, not a
+    toolchain the caller depends on.)"""
     value = os.environ.get(BACKEND_ENV, "cuda").strip().lower()
+    if value == "triton":
+        raise ValueError(
+            f"{BACKEND_ENV}=triton: tokenforge_b200 has no Triton path; use 'cuda', or 'marlin' "
+            "to keep the serving engine's own AWQ kernels"
+        )
     if value not in BACKENDS:
         raise ValueError(f"{BACKEND_ENV}={value!r} is not one of {BACKENDS}")
     return value  # type: ignore[return-value]

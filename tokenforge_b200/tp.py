@@ -18,7 +18,9 @@ is the partitioning its BASELINE configs 3 and 4 call for.
 Fused column-parallel layers (q|k|v, gate|up) are split part by part (:func:`shard_fused_columns`):
 every rank holds its slice of each projection, so a rank's gate and up columns pair up for the
 SiLU product, and with group-aligned parts its intermediate slice is exactly the K range of its
-down_proj row shard.
+down_proj row shard. A q|k|v layer that feeds real attention is split on whole heads instead
+(:func:`shard_attention`): the rank's q heads, their KV heads (replicated when there are more
+ranks than KV heads) and o_proj's K range over the same q heads.
 """
 
 from __future__ import annotations
@@ -108,15 +110,59 @@ def fused_column_bounds(parts: tuple[int, ...] | list[int], rank: int, world: in
     return out
 
 
-def shard_fused_columns(w: W4A16Weights, parts: tuple[int, ...] | list[int], rank: int, world: int,
-                        bias: torch.Tensor | None = None, group_aligned: bool = False) -> LayerShard:
-    """Column-parallel shard of a fused layer (q|k|v with parts (q, k, v); gate|up with parts
-    (I, I)): rank r holds its slice of every projection, concatenated in part order, so its
-    output is [q_r | k_r | v_r] or [gate_r | up_r]. ``group_aligned`` splits each projection in
-    whole quantization groups of columns (for gate|up, so that gate_r matches down's K shard)."""
-    if sum(parts) != w.n:
-        raise ValueError(f"parts {tuple(parts)} do not add up to N={w.n}")
-    pieces = fused_column_bounds(parts, rank, world, w.group_size if group_aligned else None)
+@dataclass(frozen=True)
+class AttentionHeads:
+    """Head layout of a grouped-query attention block. The fused q|k|v projection's output is
+    ``[q (num_heads * head_dim) | k (num_kv_heads * head_dim) | v (same)]`` and o_proj's K is
+    the attention output, ``num_heads * head_dim`` wide (Qwen2.5-7B: 28 / 4 heads of 128)."""
+
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+
+    @property
+    def parts(self) -> tuple[int, int, int]:
+        kv = self.num_kv_heads * self.head_dim
+        return (self.num_heads * self.head_dim, kv, kv)
+
+
+def attention_bounds(heads: AttentionHeads, rank: int, world: int,
+                     group_size: int | None = None) -> tuple[list[tuple[int, int]], tuple[int, int]]:
+    """Rank ``rank``'s pieces of the fused q|k|v columns (global column ranges, q then k then
+    v) and its K range of o_proj, split on whole heads so that the rank's attention output is
+    exactly the input of its o_proj shard.
+
+    The rules are the usual tensor-parallel GQA rules (vLLM's): the q heads split evenly, so
+    ``world`` must divide ``num_heads``; the KV heads split evenly when ``world <= num_kv_heads``
+    (``world`` must divide them), else each KV head is replicated on ``world / num_kv_heads``
+    consecutive ranks (``world`` must be a multiple of ``num_kv_heads``). Rank r's q heads then
+    read only its own KV heads. With ``group_size``, o's K shard must be whole groups."""
+    h, kv, hd = heads.num_heads, heads.num_kv_heads, heads.head_dim
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    if h % world:
+        raise ValueError(f"{h} attention heads do not split over {world} ranks")
+    if world <= kv:
+        if kv % world:
+            raise ValueError(f"{kv} KV heads do not split over {world} ranks")
+        k0, k1 = rank * kv // world, (rank + 1) * kv // world
+    else:
+        if world % kv:
+            raise ValueError(f"{world} ranks cannot replicate {kv} KV heads evenly")
+        k0 = rank // (world // kv)
+        k1 = k0 + 1
+    q0, q1 = rank * h // world, (rank + 1) * h // world
+    if group_size and ((q1 - q0) * hd) % group_size:
+        raise ValueError(f"o_proj's K shard of {(q1 - q0) * hd} columns is not whole groups of "
+                         f"{group_size}")
+    qw, kvw = h * hd, kv * hd
+    pieces = [(q0 * hd, q1 * hd), (qw + k0 * hd, qw + k1 * hd), (qw + kvw + k0 * hd, qw + kvw + k1 * hd)]
+    return pieces, (q0 * hd, q1 * hd)
+
+
+def shard_column_pieces(w: W4A16Weights, pieces: list[tuple[int, int]],
+                        bias: torch.Tensor | None = None) -> LayerShard:
+    """Column-parallel shard holding the given global column ranges, concatenated in order."""
     shards = [shard_columns(w, a, b) for a, b in pieces]
     weights = W4A16Weights(
         torch.cat([s.qweight_t for s in shards], dim=0),
@@ -126,6 +172,34 @@ def shard_fused_columns(w: W4A16Weights, parts: tuple[int, ...] | list[int], ran
     )
     b = None if bias is None else torch.cat([bias[a:bb] for a, bb in pieces]).contiguous()
     return LayerShard("column", weights, pieces[0], b, tuple(pieces))
+
+
+def shard_attention(qkv: W4A16Weights, o: W4A16Weights, heads: AttentionHeads, rank: int,
+                    world: int, qkv_bias: torch.Tensor | None = None,
+                    o_bias: torch.Tensor | None = None) -> tuple[LayerShard, LayerShard]:
+    """Rank ``rank``'s q|k|v and o_proj shards, split on whole heads (:func:`attention_bounds`):
+    the q|k|v shard outputs ``[q_r | k_r | v_r]`` and the o shard's K range is the columns of
+    q_r's heads."""
+    if sum(heads.parts) != qkv.n or heads.parts[0] != o.k:
+        raise ValueError(f"heads {heads} do not match q|k|v N={qkv.n} and o K={o.k}")
+    pieces, (k0, k1) = attention_bounds(heads, rank, world, o.group_size)
+    b = o_bias if (o_bias is not None and rank == 0) else None
+    return (shard_column_pieces(qkv, pieces, qkv_bias),
+            LayerShard("row", shard_rows(o, k0, k1), (k0, k1), b))
+
+
+def shard_fused_columns(w: W4A16Weights, parts: tuple[int, ...] | list[int], rank: int, world: int,
+                        bias: torch.Tensor | None = None, group_aligned: bool = False) -> LayerShard:
+    """Column-parallel shard of a fused layer (q|k|v with parts (q, k, v); gate|up with parts
+    (I, I)): rank r holds its slice of every projection, concatenated in part order, so its
+    output is [q_r | k_r | v_r] or [gate_r | up_r]. ``group_aligned`` splits each projection in
+    whole quantization groups of columns (for gate|up, so that gate_r matches down's K shard).
+    This split ignores attention heads: a q|k|v layer feeding real attention is split with
+    :func:`shard_attention` instead."""
+    if sum(parts) != w.n:
+        raise ValueError(f"parts {tuple(parts)} do not add up to N={w.n}")
+    pieces = fused_column_bounds(parts, rank, world, w.group_size if group_aligned else None)
+    return shard_column_pieces(w, pieces, bias)
 
 
 def shard_layer(
@@ -248,7 +322,7 @@ class PeerMailbox:
         import ctypes
 
         from tokenforge_b200 import _lib
-        from tokenforge_b200.ops import _aligned_rows, _check_inputs, _require
+        from tokenforge_b200.linear import _aligned_rows, _check_inputs, _require
 
         m, n, k = _check_inputs(x, w.qweight_t, w.scales, w.qzeros, w.group_size)
         for name, t in (("x", x), ("qweight_t", w.qweight_t), ("scales", w.scales),
@@ -283,7 +357,7 @@ def linear_shard(x: torch.Tensor, shard: LayerShard, group=None, linear=None,  #
     import torch.distributed as dist
 
     if linear is None:
-        from tokenforge_b200.ops import w4a16_gemm
+        from tokenforge_b200.linear import w4a16_gemm
 
         def linear(xx, w, b):  # type: ignore[no-untyped-def]
             return w4a16_gemm(xx, w.qweight_t, w.scales, w.qzeros, w.group_size, b)
