@@ -294,6 +294,61 @@ TF_API int tf_cast_e4m3(const float* in, int64_t n, uint8_t* out, void* stream);
 TF_API int tf_device_error(int* out_code);
 TF_API int tf_reset_device_error(void);
 
+/* ---------------------------------------------------------------- persistent decode chain
+ *
+ * A fixed sequence of W4A16 linears at decode sizes run as ONE persistent kernel (one CTA per
+ * SM, cooperative launch), so that the weight stream of HBM continues across layer boundaries
+ * instead of restarting at every launch. No counterpart in the reference, whose model code calls
+ * the linear op once per layer (tokenforge/kernels/ops.py:48); each op of a chain computes what
+ * tf_w4a16_linear computes for it, within the same tolerance (the K split, hence the fp32 sum
+ * order, differs), and the chain is deterministic.
+ *
+ * Limits: 1 <= M <= 8 tokens, group size 128, every N a multiple of 32 and K a multiple of 128,
+ * 16-byte aligned x / qweight_t / scales / qzeros, row strides multiples of 8 elements.
+ *
+ * `wait` nonzero: the op reads x only after every earlier op of the chain has finished (use it
+ * when x is an earlier op's output). Ops without it must not read what an earlier op writes.
+ *
+ * tf_decode_chain_create allocates the chain's device tables (tensor maps, the unit schedule,
+ * counters and the split-K partials) with cudaMalloc and synchronises the device; it records
+ * the x, weight and y addresses, so later runs read and write those same buffers.
+ * tf_decode_chain_run enqueues one launch on `stream` (graph-capturable). One chain must not run
+ * on two streams at once (its counters are per chain). tf_decode_chain_error reads and clears the
+ * chain's error word: nonzero means a bounded wait inside the kernel gave up (0x201: an op's
+ * dependency; 0x202: a weight copy) and that run's outputs are undefined.
+ */
+typedef struct TfChainOp {
+  const uint16_t* x;          /* fp16 [M, K], row stride ldx */
+  int64_t ldx;
+  const int32_t* qweight_t;   /* int32 [N, K/8] */
+  const uint16_t* scales;     /* fp16 [K/128, N] */
+  const int32_t* qzeros;      /* int32 [K/128, N/8] */
+  const uint16_t* bias;       /* fp16 [N] or NULL */
+  uint16_t* y;                /* fp16 [M, N], row stride ldy */
+  int64_t ldy;
+  int64_t N, K;
+  int32_t wait;
+  int32_t reserved;
+} TfChainOp;
+
+typedef struct TfChain TfChain;
+
+TF_API int tf_decode_chain_create(const TfChainOp* ops, int32_t n_ops, int64_t M,
+                                  int32_t group_size, TfChain** out);
+TF_API int tf_decode_chain_run(TfChain* chain, void* stream);
+TF_API int tf_decode_chain_error(TfChain* chain, int* out_code);
+TF_API int tf_decode_chain_destroy(TfChain* chain);
+
+/* The unit schedule tf_decode_chain_create would build for these shapes on `num_ctas` SMs
+ * (host only, no GPU needed): one record per unit, in per-CTA order. Returns TF_ERR_TOO_LARGE
+ * when `capacity` records do not hold them (n_units is set either way). */
+typedef struct TfChainUnitInfo {
+  int32_t cta, op, tile0, rtiles, c0, c1, piece, pieces, flags;
+} TfChainUnitInfo;
+TF_API int tf_decode_chain_plan(const int64_t* n, const int64_t* k, int32_t n_ops, int64_t M,
+                                int32_t num_ctas, TfChainUnitInfo* out, int32_t capacity,
+                                int32_t* n_units);
+
 #ifdef __cplusplus
 }
 #endif

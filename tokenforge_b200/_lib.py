@@ -91,6 +91,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tf_cast_e4m3": (ctypes.c_int, [_P, _I64, _P, _P]),
     "tf_device_error": (ctypes.c_int, [_P]),
     "tf_reset_device_error": (ctypes.c_int, []),
+    "tf_decode_chain_create": (ctypes.c_int, [_P, _I32, _I64, _I32, _P]),
+    "tf_decode_chain_run": (ctypes.c_int, [_P, _P]),
+    "tf_decode_chain_error": (ctypes.c_int, [_P, _P]),
+    "tf_decode_chain_destroy": (ctypes.c_int, [_P]),
+    "tf_decode_chain_plan": (ctypes.c_int, [_P, _P, _I32, _I64, _I32, _P, _I32, _P]),
 }
 
 TF_MAX_PEERS = 8
@@ -107,6 +112,32 @@ class TfPeerSet(ctypes.Structure):
         ("max_n", ctypes.c_int32),
         ("mailbox", ctypes.c_void_p * TF_MAX_PEERS),
     ]
+
+
+class TfChainOp(ctypes.Structure):
+    """Mirror of ``TfChainOp`` in include/tokenforge_b200.h."""
+
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("ldx", ctypes.c_int64),
+        ("qweight_t", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+        ("qzeros", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("ldy", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("wait", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
+class TfChainUnitInfo(ctypes.Structure):
+    """Mirror of ``TfChainUnitInfo`` in include/tokenforge_b200.h."""
+
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("cta", "op", "tile0", "rtiles", "c0", "c1", "piece", "pieces", "flags")]
 
 
 _lock = threading.Lock()
