@@ -103,75 +103,81 @@ __device__ __forceinline__ void mma_16816_zc(float (&d)[4], const uint32_t (&a)[
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
 }
 
-// Group-size-128 block (one K block is one quantization group): the scale moves out of the
-// per-weight work. Each pair is unpacked to the exact fp16 integer pair (q - z): bits 0-3 of a
-// half ORed into 0x6400 read as 1024 + q and bits 4-7 ORed into 0x5400 read as 64 + q, so one
-// LOP3 and one HSUB2 of (1024 + z) or (64 + z) give q - z for either nibble position (one shift
-// per word brings the upper byte of each half down). The tensor core sums x * (q - z) exactly
-// into fp32 and the block's sum is multiplied by the row's scale once: no fp16 weight is rounded,
-// q == z contributes exactly zero, and Inf / NaN activations propagate as through the dequant.
-__device__ __forceinline__ void gcompute_grp(float (&acc)[2][2][4], const GSlot& s, int bb,
-                                             const GLane& L) {
+// The four rows' zero points of a group-size-128 block as fp16x2 broadcasts: z0[j] = (1024 + z_j)
+// twice and z1[j] = (64 + z_j) twice. The rows' zero points sit in nibbles {0, 4, 1, 5} of the
+// qzeros word shifted by nib[0] (0 or 8): one LOP3 per row pair gives (1024 + z_a, 1024 + z_b),
+// a byte permute broadcasts each row's value, and 1024 + z - 960 = 64 + z exactly.
+__device__ __forceinline__ void zero_points(uint32_t (&z0)[4], uint32_t (&z1)[4], uint32_t zword,
+                                            int nib0) {
+  const uint32_t zs = zword >> nib0;
+  const uint32_t a = lop_mask_or(zs, 0x000F000Fu, 0x64006400u);
+  const uint32_t b = lop_mask_or(zs >> 4, 0x000F000Fu, 0x64006400u);
+  z0[0] = __byte_perm(a, a, 0x1010u);
+  z0[1] = __byte_perm(a, a, 0x3232u);
+  z0[2] = __byte_perm(b, b, 0x1010u);
+  z0[3] = __byte_perm(b, b, 0x3232u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
+}
+
+// The lane's 4 x 16 dequantized fp16x2 pairs of one word column i of a group-size-128 block, in
+// the MMA fragment order: each pair is unpacked to the exact fp16 integers (q - z) (bits 0-3 of
+// a half ORed into 0x6400 read as 1024 + q, bits 4-7 ORed into 0x5400 as 64 + q; one LOP3, one
+// shift per word for the upper byte, one HSUB2 of (1024 + z) or (64 + z)) and multiplied by the
+// row's scale with one HMUL2: w = fp16((q - z) * s), one rounding, the reference's dequantized
+// weight (tokenforge/kernels/pack.py:189-194), so the tensor core's fp32 sums are those of the
+// reference's fp16 weights and Inf / NaN follow the reference's dequant.
+struct W16Frag {
+  uint32_t t0a[4], t0b[4], t1a[4], t1b[4];  // tile 0 / 1, k offsets (0..3) / (4..7) of the word
+};
+
+__device__ __forceinline__ void dequant_word(W16Frag& f, const uint32_t (&w)[4],
+                                             const uint32_t (&z0)[4], const uint32_t (&z1)[4],
+                                             const uint32_t (&sc)[4]) {
   const uint32_t m0 = 0x000F000Fu, m1 = 0x00F000F0u;
   const uint32_t g0 = 0x64006400u, g1 = 0x54005400u;
-  // The four rows' zero points sit in nibbles {0, 4, 1, 5} of the qzeros word shifted by nib[0]
-  // (0 or 8): one LOP3 per row pair gives (1024 + z_a, 1024 + z_b), a byte permute broadcasts each
-  // row's value to both halves, and 1024 + z - 960 = 64 + z exactly.
-  uint32_t z0[4], z1[4];
-  {
-    const uint32_t zs = s.z >> L.nib[0];
-    const uint32_t a = lop_mask_or(zs, m0, g0), b = lop_mask_or(zs >> 4, m0, g0);
-    z0[0] = __byte_perm(a, a, 0x1010u);
-    z0[1] = __byte_perm(a, a, 0x3232u);
-    z0[2] = __byte_perm(b, b, 0x1010u);
-    z0[3] = __byte_perm(b, b, 0x3232u);
+  uint32_t pa[4], pb[4], pc[4], pd[4];  // offsets (0,1), (2,3), (4,5), (6,7) of row j's word
 #pragma unroll
-    for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t h = w[j] >> 8;
+    pa[j] = hmul2_rn(hsub2_rn(lop_mask_or(w[j], m0, g0), z0[j]), sc[j]);
+    pb[j] = hmul2_rn(hsub2_rn(lop_mask_or(w[j], m1, g1), z1[j]), sc[j]);
+    pc[j] = hmul2_rn(hsub2_rn(lop_mask_or(h, m0, g0), z0[j]), sc[j]);
+    pd[j] = hmul2_rn(hsub2_rn(lop_mask_or(h, m1, g1), z1[j]), sc[j]);
   }
+  // Tile 0: fragment rows q / q+8 <- rows 4q / 4q+1; tile 1 <- rows 4q+2 / 4q+3.
+  f.t0a[0] = pa[0]; f.t0a[1] = pa[1]; f.t0a[2] = pb[0]; f.t0a[3] = pb[1];
+  f.t0b[0] = pc[0]; f.t0b[1] = pc[1]; f.t0b[2] = pd[0]; f.t0b[3] = pd[1];
+  f.t1a[0] = pa[2]; f.t1a[1] = pa[3]; f.t1a[2] = pb[2]; f.t1a[3] = pb[3];
+  f.t1b[0] = pc[2]; f.t1b[1] = pc[3]; f.t1b[2] = pd[2]; f.t1b[3] = pd[3];
+}
+
+// (s, s) broadcasts of the lane's four rows' scales.
+__device__ __forceinline__ void scale_pairs(uint32_t (&sc)[4], const GSlot& s) {
+  sc[0] = __byte_perm(s.s.x, s.s.x, 0x1010u);
+  sc[1] = __byte_perm(s.s.x, s.s.x, 0x3232u);
+  sc[2] = __byte_perm(s.s.y, s.s.y, 0x1010u);
+  sc[3] = __byte_perm(s.s.y, s.s.y, 0x3232u);
+}
+
+// acc += x * w over one group-size-128 block bb, w dequantized per weight as the reference
+// does (dequant_word); acc[t][i % 2] are two independent accumulator chains per row tile.
+__device__ __forceinline__ void gcompute_w16(float (&acc)[2][2][4], const GSlot& s, int bb,
+                                             const GLane& L) {
+  uint32_t z0[4], z1[4], sc[4];
+  zero_points(z0, z1, s.z, L.nib[0]);
+  scale_pairs(sc, s);
   const uint4* xp = L.xs + (bb - L.kb0) * (kKB / 8);
-  const uint32_t w[4][4] = {{s.w[0].x, s.w[0].y, s.w[0].z, s.w[0].w},
-                            {s.w[1].x, s.w[1].y, s.w[1].z, s.w[1].w},
-                            {s.w[2].x, s.w[2].y, s.w[2].z, s.w[2].w},
-                            {s.w[3].x, s.w[3].y, s.w[3].z, s.w[3].w}};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint4 xv = xp[i];
-    uint32_t pa[4], pb[4], pc[4], pd[4];  // offsets (0,1), (2,3), (4,5), (6,7) of row j's word i
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t h = w[j][i] >> 8;
-      pa[j] = hsub2_rn(lop_mask_or(w[j][i], m0, g0), z0[j]);
-      pb[j] = hsub2_rn(lop_mask_or(w[j][i], m1, g1), z1[j]);
-      pc[j] = hsub2_rn(lop_mask_or(h, m0, g0), z0[j]);
-      pd[j] = hsub2_rn(lop_mask_or(h, m1, g1), z1[j]);
-    }
-    // Tile 0: fragment rows q / q+8 <- rows 4q / 4q+1; tile 1 <- rows 4q+2 / 4q+3.
-    const uint32_t t0a[4] = {pa[0], pa[1], pb[0], pb[1]}, t0b[4] = {pc[0], pc[1], pd[0], pd[1]};
-    const uint32_t t1a[4] = {pa[2], pa[3], pb[2], pb[3]}, t1b[4] = {pc[2], pc[3], pd[2], pd[3]};
-    if (i == 0) {
-      mma_16816_zc(acc[0][0], t0a, xv.x, xv.y);
-      mma_16816_zc(acc[1][0], t1a, xv.x, xv.y);
-    } else {
-      mma_16816(acc[0][0], t0a, xv.x, xv.y);
-      mma_16816(acc[1][0], t1a, xv.x, xv.y);
-    }
-    mma_16816(acc[0][0], t0b, xv.z, xv.w);
-    mma_16816(acc[1][0], t1b, xv.z, xv.w);
-  }
-}
-
-// y += s * (block sum, one accumulator chain per tile) for the lane's four rows (row 4q + j: tile j / 2, fragment values
-// 2 (j % 2) and 2 (j % 2) + 1, tokens 2c and 2c + 1).
-__device__ __forceinline__ void fold_grp(float (&y)[2][4], const float (&acc)[2][2][4],
-                                         const GSlot& s) {
-  const uint32_t sp[2] = {s.s.x, s.s.y};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t sh = (j & 1) ? (sp[j >> 1] >> 16) : (sp[j >> 1] & 0xFFFFu);
-    const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sh)));
-    const int t = j >> 1, e = 2 * (j & 1);
-    y[t][e] = fmaf(sf, acc[t][0][e], y[t][e]);
-    y[t][e + 1] = fmaf(sf, acc[t][0][e + 1], y[t][e + 1]);
+    const uint32_t w[4] = {(&s.w[0].x)[i], (&s.w[1].x)[i], (&s.w[2].x)[i], (&s.w[3].x)[i]};
+    W16Frag f;
+    dequant_word(f, w, z0, z1, sc);
+    mma_16816(acc[0][i & 1], f.t0a, xv.x, xv.y);
+    mma_16816(acc[1][i & 1], f.t1a, xv.x, xv.y);
+    mma_16816(acc[0][i & 1], f.t0b, xv.z, xv.w);
+    mma_16816(acc[1][i & 1], f.t1b, xv.z, xv.w);
   }
 }
 

@@ -58,8 +58,12 @@ constexpr int kTileRows = 32;                 // weight rows per row tile
 constexpr int kWBytes = kTileRows * 128;      // packed weights of a chunk: 32 rows x 128 bytes
 constexpr int kSBytes = 2 * kTileRows * 2;    // scales: [2 groups][32 rows] fp16
 constexpr int kZBytes = 2 * 4 * 4;            // zero points: [2 groups][4 words]
-constexpr int kSZBytes = kSBytes + kZBytes;
+// A slot's scale and zero-point boxes each start on a 128-byte boundary (the alignment TMA
+// requires of a shared-memory destination).
+constexpr int kSZBytes = 256;
+constexpr int kZOffInSZ = 128;
 constexpr uint32_t kTxBytes = kWBytes + kSBytes + kZBytes;
+static_assert(kSBytes <= kZOffInSZ && kZOffInSZ + kZBytes <= kSZBytes, "scale/zero slot layout");
 constexpr int kMaxM = 8;
 constexpr int kRedFloats = 8 * 32;            // per warp: 8 fragment values x 32 lanes
 constexpr unsigned long long kChainWaitNs = 2000000000ull;
@@ -73,6 +77,9 @@ constexpr int kOffMisc = kOffRed + kWarps * kRedFloats * 4;
 constexpr int kOffX = kOffMisc + 64;
 constexpr int kSmemCap = 227 * 1024;
 constexpr int kAlignSlack = 1024;
+static_assert(kOffW % 1024 == 0 && kWBytes % 1024 == 0, "128-byte-swizzled boxes need 1 KB alignment");
+static_assert(kOffSZ % 128 == 0 && kSZBytes % 128 == 0, "TMA destinations need 128-byte alignment");
+static_assert(kOffBar % 8 == 0 && kOffRed % 16 == 0 && kOffX % 16 == 0, "shared-memory alignment");
 
 // Error codes recorded in the chain's error word (first one wins).
 constexpr uint32_t kErrDepWait = 0x201;    // an op's dependency counter did not complete in time
@@ -85,9 +92,6 @@ struct alignas(64) ChainOpDev {
   const __half* x;
   const __half* bias;
   __half* y;
-  const int32_t* qw;  // the same tensors by address, for the rare non-finite recompute
-  const __half* scales;
-  const int32_t* qzeros;
   int64_t ldx, ldy;
   int32_t n, k, wait, tiles;
 };
@@ -191,7 +195,7 @@ __device__ __forceinline__ void issue_chunk(const ChainParams& p, uint8_t* smem,
   const ChainOpDev* o = p.ops + op;
   tma_load_2d(wdst, &o->mw, bar, chunk * 32, tile * kTileRows);
   tma_load_2d(szdst, &o->ms, bar, tile * kTileRows, chunk * 2);
-  tma_load_2d(szdst + kSBytes, &o->mz, bar, tile * 4, chunk * 2);
+  tma_load_2d(szdst + kZOffInSZ, &o->mz, bar, tile * 4, chunk * 2);
 }
 
 // Block b (0 or 1) of a chunk in the ring as this lane's GSlot: rows 4q..4q+3, 16 bytes each at
@@ -205,27 +209,7 @@ __device__ __forceinline__ void ring_block(GSlot& s, const uint8_t* w, const uin
     s.w[j] = *reinterpret_cast<const uint4*>(w + row * 128 + phys * 16);
   }
   s.s = *reinterpret_cast<const uint2*>(sz + b * 64 + q * 8);
-  s.z = *reinterpret_cast<const uint32_t*>(sz + kSBytes + b * 16 + (q >> 1) * 4);
-}
-
-// The same block read from global memory (the non-finite recompute). Past K: zero weights,
-// scales and zero points, as the TMA fill gives.
-__device__ __forceinline__ void global_block(GSlot& s, const ChainOpDev& o, int tile, int chunk,
-                                             int b, int q, int c) {
-  const int k = chunk * kChunkK + b * kKB + 32 * c;
-  const int row0 = tile * kTileRows + 4 * q;
-  if (k >= o.k) {
-    s.w[0] = s.w[1] = s.w[2] = s.w[3] = make_uint4(0, 0, 0, 0);
-    s.s = make_uint2(0u, 0u);
-    s.z = 0u;
-    return;
-  }
-  const int g = k >> 7;
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    s.w[j] = __ldg(reinterpret_cast<const uint4*>(o.qw + static_cast<int64_t>(row0 + j) * (o.k / 8) + k / 8));
-  s.s = __ldg(reinterpret_cast<const uint2*>(o.scales + static_cast<int64_t>(g) * o.n + row0));
-  s.z = static_cast<uint32_t>(__ldg(o.qzeros + static_cast<int64_t>(g) * (o.n / 8) + row0 / 8));
+  s.z = *reinterpret_cast<const uint32_t*>(sz + kZOffInSZ + b * 16 + (q >> 1) * 4);
 }
 
 // Stages x[0:M, c0 * 256 : c1 * 256] (zero past K) into shared memory, rows x_stride apart, with
@@ -312,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
   int arrived = -1;  // ops whose arrival this CTA has published
   int passed = -1;   // the CTA has waited for every op before `passed`
   const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
-  float ytot[2][4] = {};
+  float acc[2][2][4] = {};  // x * fp16((q - z) * s) in fp32: two chains per row tile
   bool timed_out = false;
 
   for (int u = u_begin; u < u_end; ++u) {
@@ -353,15 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
 #pragma unroll
       for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) ytot[t][r] = 0.f;
+        for (int r = 0; r < 4; ++r) acc[t][0][r] = acc[t][1][r] = 0.f;
     }
     GLane L;
     L.c = c;
     L.kb0 = 2 * U.c0;
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) L.nib[jj] = 4 * awq_nibble_of((4 * q + jj) & 7);
+    L.nib[0] = (q & 1) ? 8 : 0;  // rows 4q..4q+3: zero points in nibbles {0,4,1,5} or {2,6,3,7}
     L.xs = xs4 + (min(q, p.M - 1) * p.x_stride + 32 * c) / 8;
-    float ysub[2][4] = {};
     if (tile_ok) {
       for (int ch = U.c0 + j; ch < U.c1; ch += P) {
         top_up(consumed);
@@ -373,38 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
         for (int b = 0; b < 2; ++b) {
           GSlot s;
           ring_block(s, wt, sz, b, q, c);
-          float acc[2][2][4];
-          gcompute_grp(acc, s, 2 * ch + b, L);
-          fold_grp(ysub, acc, s);
+          gcompute_w16(acc, s, 2 * ch + b, L);
         }
         ++consumed;
       }
-      // A non-finite sum: recompute the warp's chunks of this unit with the per-weight dequant
-      // fp16(q - z) * s, whose Inf / NaN pattern is the reference's.
-      bool bad = false;
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) bad |= !isfinite(ysub[t][r]);
-      if (__any_sync(0xffffffffu, bad)) {
-        float acc[2][2][4] = {};
-        const uint32_t mask = 0x000F000Fu, magic = 0x64006400u;
-        for (int ch = U.c0 + j; ch < U.c1; ch += P)
-          for (int b = 0; b < 2; ++b) {
-            GSlot s;
-            global_block(s, o, tile, ch, b, q, c);
-            gcompute(acc, s, 2 * ch + b, L, mask, magic);
-          }
-#pragma unroll
-        for (int t = 0; t < 2; ++t)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) ysub[t][r] = acc[t][0][r] + acc[t][1][r];
-      }
     }
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) ytot[t][r] += ysub[t][r];
     if (!(U.flags & kLast)) continue;
 
     // Reduce the P warps of each row tile in warp order, then write (or hand the piece over).
@@ -412,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) mine[(t * 4 + r) * 32 + lane] = ytot[t][r];
+      for (int r = 0; r < 4; ++r) mine[(t * 4 + r) * 32 + lane] = acc[t][0][r] + acc[t][1][r];
     __syncthreads();
     if (j != 0 || !tile_ok) continue;
     float v[2][4];
@@ -709,9 +664,6 @@ int tf_decode_chain_create(const TfChainOp* ops, int32_t n_ops, int64_t M, int32
     d.x = reinterpret_cast<const __half*>(s.x);
     d.bias = reinterpret_cast<const __half*>(s.bias);
     d.y = reinterpret_cast<__half*>(s.y);
-    d.qw = s.qweight_t;
-    d.scales = reinterpret_cast<const __half*>(s.scales);
-    d.qzeros = s.qzeros;
     d.ldx = s.ldx;
     d.ldy = s.ldy;
     d.n = static_cast<int32_t>(s.N);

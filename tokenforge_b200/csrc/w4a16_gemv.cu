@@ -26,8 +26,9 @@
 //     it hid); the first loads are issued before the programmatic-dependent-launch wait;
 //   * rows beyond N and tokens beyond M are clamped for loading (never stored); only a partial
 //     last K block takes predicated loads;
-//   * unpack and dequant are PTX (lop3, sub.rn / mul.rn.f16x2): exactly three instructions per
-//     fp16 pair plus three shifts per packed word, bit-exact with the reference dequant.
+//   * unpack and dequant are PTX (lop3, sub.rn / mul.rn.f16x2): three instructions per fp16 pair
+//     plus one shift per packed word at group size 128 (bits 4-7 of each half unpack through the
+//     0x5400 magic), bit-exact with the reference dequant.
 // The dequantized pairs feed the tensor core directly (the k order inside an MMA step only has to
 // agree between the A and B fragments); it performs the fp32 multiply-accumulate, four
 // independent accumulator chains per lane.
@@ -519,15 +520,13 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
   __syncthreads();
   if constexpr (kNorm) norm_quant_staged(p, xs_smem, red, norm_scale_sh);
 
+  // Group size 128 (kFact): the scale and zero point are loaded once per block and every weight
+  // is dequantized as the reference does (gcompute_w16); other group sizes look up the group of
+  // every word (gcompute). Both sum x * fp16((q - z) * s) on the tensor core in fp32.
   float acc[2][2][4] = {};
-  float y[2][4] = {};
   auto step = [&](const GSlot& sl, int b) {
-    if constexpr (kFact) {
-      gcompute_grp(acc, sl, b, L);
-      fold_grp(y, acc, sl);
-    } else {
-      gcompute(acc, sl, b, L, mask, magic);
-    }
+    if constexpr (kFact) gcompute_w16(acc, sl, b, L);
+    else gcompute(acc, sl, b, L, mask, magic);
   };
   for (int b = b0; b < L.b_end; b += 2) {
     step(s0, b);
@@ -535,38 +534,6 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
     if (b + 1 >= L.b_end) break;
     step(s1, b + 1);
     load(s1, b + 3);
-  }
-  if constexpr (kFact) {
-    // A non-finite activation or scale makes some y non-finite (fp32 sums of finite fp16
-    // products cannot overflow). Then the warp recomputes its range with the per-weight dequant
-    // fp16(q - z) * s, whose Inf / NaN pattern is the reference's (an Inf scale times q == z is
-    // NaN there, while the block-scaled sum would give Inf).
-    bool bad = false;
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) bad |= !isfinite(y[t][r]);
-    if (__any_sync(0xffffffffu, bad)) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[t][0][r] = acc[t][1][r] = 0.f;
-      for (int b = b0; b < L.b_end; ++b) {
-        gload_grp(s0, b, p, L);
-        gcompute(acc, s0, b, L, mask, magic);
-      }
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) y[t][r] = acc[t][0][r] + acc[t][1][r];
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        acc[t][0][r] = y[t][r];
-        acc[t][1][r] = 0.f;
-      }
   }
 
   // Fixed-order reductions: the accumulator chains, then the WARPS_K warps (warp order), then the
@@ -648,75 +615,33 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, kWideWarps / (WARPS_N 
 }
 
 // ---------------------------------------------------------------- 16-token decode GEMV
-// M = 9..16 with group size 128: the M <= 8 kernel's weight streaming and exact (q - z) unpack,
-// with every unpacked block fed to two 8-token MMA n-tiles (tokens 0-7 and 8-15), so the unpack
-// work of a weight is shared by sixteen tokens instead of eight. The accumulators of both
+// M = 9..16 with group size 128: the M <= 8 kernel's weight streaming and per-weight dequant,
+// with every dequantized block fed to two 8-token MMA n-tiles (tokens 0-7 and 8-15), so the
+// dequant work of a weight is shared by sixteen tokens instead of eight. The accumulators of both
 // n-tiles double the per-thread state, so this kernel runs 8-warp CTAs at two per SM with the
 // register budget that allows; the K split (warps, cluster DSMEM, cross-cluster partials) and
 // every sum order are the M <= 8 kernel's.
-__device__ __forceinline__ void gcompute_grp2(float (&a0)[2][4], float (&a1)[2][4], const GSlot& s,
-                                              int bb, const GLane& L, const uint4* xs1) {
-  const uint32_t m0 = 0x000F000Fu, m1 = 0x00F000F0u;
-  const uint32_t g0 = 0x64006400u, g1 = 0x54005400u;
-  uint32_t z0[4], z1[4];
-  {
-    const uint32_t zs = s.z >> L.nib[0];
-    const uint32_t a = lop_mask_or(zs, m0, g0), b = lop_mask_or(zs >> 4, m0, g0);
-    z0[0] = __byte_perm(a, a, 0x1010u);
-    z0[1] = __byte_perm(a, a, 0x3232u);
-    z0[2] = __byte_perm(b, b, 0x1010u);
-    z0[3] = __byte_perm(b, b, 0x3232u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
-  }
+__device__ __forceinline__ void gcompute_w16_2(float (&a0)[2][4], float (&a1)[2][4], const GSlot& s,
+                                               int bb, const GLane& L, const uint4* xs1) {
+  uint32_t z0[4], z1[4], sc[4];
+  zero_points(z0, z1, s.z, L.nib[0]);
+  scale_pairs(sc, s);
   const uint4* xp0 = L.xs + (bb - L.kb0) * (kKB / 8);
   const uint4* xp1 = xs1 + (bb - L.kb0) * (kKB / 8);
-  const uint32_t w[4][4] = {{s.w[0].x, s.w[0].y, s.w[0].z, s.w[0].w},
-                            {s.w[1].x, s.w[1].y, s.w[1].z, s.w[1].w},
-                            {s.w[2].x, s.w[2].y, s.w[2].z, s.w[2].w},
-                            {s.w[3].x, s.w[3].y, s.w[3].z, s.w[3].w}};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint4 xv0 = xp0[i], xv1 = xp1[i];
-    uint32_t pa[4], pb[4], pc[4], pd[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t h = w[j][i] >> 8;
-      pa[j] = hsub2_rn(lop_mask_or(w[j][i], m0, g0), z0[j]);
-      pb[j] = hsub2_rn(lop_mask_or(w[j][i], m1, g1), z1[j]);
-      pc[j] = hsub2_rn(lop_mask_or(h, m0, g0), z0[j]);
-      pd[j] = hsub2_rn(lop_mask_or(h, m1, g1), z1[j]);
-    }
-    const uint32_t t0a[4] = {pa[0], pa[1], pb[0], pb[1]}, t0b[4] = {pc[0], pc[1], pd[0], pd[1]};
-    const uint32_t t1a[4] = {pa[2], pa[3], pb[2], pb[3]}, t1b[4] = {pc[2], pc[3], pd[2], pd[3]};
-    if (i == 0) {
-      mma_16816_zc(a0[0], t0a, xv0.x, xv0.y);
-      mma_16816_zc(a0[1], t1a, xv0.x, xv0.y);
-      mma_16816_zc(a1[0], t0a, xv1.x, xv1.y);
-      mma_16816_zc(a1[1], t1a, xv1.x, xv1.y);
-    } else {
-      mma_16816(a0[0], t0a, xv0.x, xv0.y);
-      mma_16816(a0[1], t1a, xv0.x, xv0.y);
-      mma_16816(a1[0], t0a, xv1.x, xv1.y);
-      mma_16816(a1[1], t1a, xv1.x, xv1.y);
-    }
-    mma_16816(a0[0], t0b, xv0.z, xv0.w);
-    mma_16816(a0[1], t1b, xv0.z, xv0.w);
-    mma_16816(a1[0], t0b, xv1.z, xv1.w);
-    mma_16816(a1[1], t1b, xv1.z, xv1.w);
-  }
-}
-
-// y += s * block sum for one n-tile (accumulator per row tile; layout as fold_grp).
-__device__ __forceinline__ void fold_grp1(float (&y)[2][4], const float (&a)[2][4], const GSlot& s) {
-  const uint32_t sp[2] = {s.s.x, s.s.y};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t sh = (j & 1) ? (sp[j >> 1] >> 16) : (sp[j >> 1] & 0xFFFFu);
-    const float sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sh)));
-    const int t = j >> 1, e = 2 * (j & 1);
-    y[t][e] = fmaf(sf, a[t][e], y[t][e]);
-    y[t][e + 1] = fmaf(sf, a[t][e + 1], y[t][e + 1]);
+    const uint32_t w[4] = {(&s.w[0].x)[i], (&s.w[1].x)[i], (&s.w[2].x)[i], (&s.w[3].x)[i]};
+    W16Frag f;
+    dequant_word(f, w, z0, z1, sc);
+    mma_16816(a0[0], f.t0a, xv0.x, xv0.y);
+    mma_16816(a0[1], f.t1a, xv0.x, xv0.y);
+    mma_16816(a1[0], f.t0a, xv1.x, xv1.y);
+    mma_16816(a1[1], f.t1a, xv1.x, xv1.y);
+    mma_16816(a0[0], f.t0b, xv0.z, xv0.w);
+    mma_16816(a0[1], f.t1b, xv0.z, xv0.w);
+    mma_16816(a1[0], f.t0b, xv1.z, xv1.w);
+    mma_16816(a1[1], f.t1b, xv1.z, xv1.w);
   }
 }
 
@@ -750,7 +675,6 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, 2) w4a16_gemv16_kernel
   for (int j = 0; j < 4; ++j) L.nib[j] = 4 * awq_nibble_of((r0 + j) & 7);
   L.xs = xs_smem + (min(q, p.M - 1) * p.xs_stride + 32 * L.c) / 8;
   const uint4* xs1 = xs_smem + (min(q + 8, p.M - 1) * p.xs_stride + 32 * L.c) / 8;
-  const uint32_t mask = 0x000F000Fu, magic = 0x64006400u;
 
   GSlot s0, s1;
   gload_grp(s0, b0, p, L);
@@ -760,43 +684,13 @@ __global__ void __launch_bounds__(32 * WARPS_N * WARPS_K, 2) w4a16_gemv16_kernel
   stage_activations(p, xs_smem, L.kb0, kb1);
   __syncthreads();
 
-  float a0[2][4], a1[2][4];
-  float y[2][2][4] = {};  // [n-tile][row tile][value]
+  float y[2][2][4] = {};  // [n-tile][row tile][value]: x * fp16((q - z) * s) summed in fp32
   for (int b = b0; b < L.b_end; b += 2) {
-    gcompute_grp2(a0, a1, s0, b, L, xs1);
-    fold_grp1(y[0], a0, s0);
-    fold_grp1(y[1], a1, s0);
+    gcompute_w16_2(y[0], y[1], s0, b, L, xs1);
     gload_grp(s0, b + 2, p, L);
     if (b + 1 >= L.b_end) break;
-    gcompute_grp2(a0, a1, s1, b + 1, L, xs1);
-    fold_grp1(y[0], a0, s1);
-    fold_grp1(y[1], a1, s1);
+    gcompute_w16_2(y[0], y[1], s1, b + 1, L, xs1);
     gload_grp(s1, b + 3, p, L);
-  }
-  // A non-finite y: the warp recomputes its range with the per-weight dequant (the M <= 8
-  // kernel's rule), each n-tile in turn.
-  bool bad = false;
-#pragma unroll
-  for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) bad |= !isfinite(y[nt][t][r]);
-  if (__any_sync(0xffffffffu, bad)) {
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      GLane Ln = L;
-      if (nt == 1) Ln.xs = xs1;
-      float acc[2][2][4] = {};
-      for (int b = b0; b < L.b_end; ++b) {
-        gload_grp(s0, b, p, Ln);
-        gcompute(acc, s0, b, Ln, mask, magic);
-      }
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) y[nt][t][r] = acc[t][0][r] + acc[t][1][r];
-    }
   }
 
   // Fixed-order reductions: the WARPS_K warps (warp order), then the cluster's CTAs (rank order).
