@@ -409,6 +409,198 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _median_seconds(fn, min_seconds: float) -> tuple[float, int]:  # type: ignore[no-untyped-def]
+    fn()  # first touch
+    times: list[float] = []
+    while len(times) < 3 or sum(times) < min_seconds:
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def cpu_aux_baselines(min_seconds: float = 4.0) -> dict[str, dict]:
+    """The reference's CPU path for the other legs, through the oracle's C ports on bounded samples:
+    the GEMM (w4a16_torch, reference.py:24-32, at M = 1024 on a 1024-column slice of gate_up),
+    the AWQ repack (repack_awq_to_tf, pack.py:141-143, on the whole down layer) and RMSNorm + FP8
+    (rmsnorm_fp8_reference, reference.py:53-56, at T = 4096, H = 3584)."""
+    from oracle import oracle
+
+    cores = os.cpu_count() or 1
+    gen = torch.Generator().manual_seed(11)
+    out: dict[str, dict] = {}
+    m, n, k = 1024, 1024, HIDDEN
+    qw = torch.randint(-(2**31), 2**31 - 1, (n, k // 8), generator=gen, dtype=torch.int32)
+    z = torch.randint(-(2**31), 2**31 - 1, (k // G, n // 8), generator=gen, dtype=torch.int32)
+    s = (torch.rand((k // G, n), generator=gen) * 0.018 + 0.002).to(torch.float16)
+    x = torch.randn((m, k), generator=gen).to(torch.float16)
+    sec, reps = _median_seconds(lambda: oracle.w4a16_cpu(x, qw, s, z, G, threads=cores), min_seconds)
+    out["gemm"] = {"value": round(2 * m * n * k / sec / 1e12, 5), "unit": "TFLOP/s", "cores": cores,
+                   "kind": "port", "sample": f"w4a16_torch at M={m}, N={n} (a slice of gate_up), "
+                                             f"K={k}; median of {reps}"}
+    qweight = torch.randint(-(2**31), 2**31 - 1, (INTER, HIDDEN // 8), generator=gen,
+                            dtype=torch.int32)
+    sec, reps = _median_seconds(lambda: oracle.repack_awq_to_tf(qweight), min_seconds)
+    out["repack"] = {"value": round(2 * qweight.numel() * 4 / sec / 1e9, 4), "unit": "GB/s",
+                     "cores": 1, "kind": "port",
+                     "sample": f"repack_awq_to_tf of down [{INTER}, {HIDDEN // 8}] int32, one "
+                               f"thread; median of {reps}"}
+    t = 4096
+    xr = torch.randn((t, HIDDEN), generator=gen).to(torch.float16)
+    gamma = (1 + 0.1 * torch.randn(HIDDEN, generator=gen)).to(torch.float16)
+    sec, reps = _median_seconds(lambda: oracle.rmsnorm_fp8(xr, gamma, 1e-6), min_seconds)
+    per_call = t * HIDDEN * 2 + HIDDEN * 2 + t * HIDDEN + t * 4
+    out["rmsnorm_fp8"] = {"value": round(per_call / sec / 1e9, 4), "unit": "GB/s", "cores": cores,
+                          "kind": "port",
+                          "sample": f"rmsnorm_fp8_reference at T={t}, H={HIDDEN}; median of {reps}"}
+    return out
+
+
+def _w4a16_tol(x: torch.Tensor, w16: torch.Tensor) -> float:
+    """The W4A16 tolerance rule c * sqrt(K) * 2^-10 * max|x| * max|w| with the calibrated cuda
+    constant (tests/numerics/tolerances.json), the reference's rule (tests/numerics/tolerance.py)."""
+    c = json.loads((ROOT / "tests" / "numerics" / "tolerances.json").read_text())["w4a16"]["cuda"]["c"]
+    return float(c) * x.shape[-1] ** 0.5 * 2.0**-10 * float(x.abs().max()) * float(w16.abs().max())
+
+
+def decode_parity(device: torch.device, rank: int, world: int, peers, m: int) -> dict:  # type: ignore[no-untyped-def]
+    """Correctness of the timed decode paths at this N, checked in the bench run itself with the
+    product's own kernels: the o and down layers of Qwen2.5-7B (weights from one seed, identical
+    on every rank) against the fp64 product of their dequantized weights (tokenforge dequant
+    kernel, bit-exact with the reference's dequant), full width.
+      N = 1: the decode GEMV (tf_w4a16_linear) of each layer within the W4A16 tolerance.
+      N > 1: each rank's row shard through the all-reduce fused into the GEMV
+      (tf_w4a16_linear_allreduce) and through the GEMV + NCCL all-reduce; the fused result must
+      be bit-identical on every rank and across repeated calls, within the tolerance of the
+      fp64 product of the unsharded layer (NCCL path: twice the tolerance, fp16 partials)."""
+    import torch.distributed as dist
+
+    import tokenforge_b200.ops as ops
+    from tokenforge_b200 import tp
+
+    gen = torch.Generator(device=device).manual_seed(2027)
+    res: dict[str, object] = {"m": m, "layers": {}}
+    ok = True
+    for name, n, k in (("o", HIDDEN, HIDDEN), ("down", HIDDEN, INTER)):
+        w = random_w4a16(n, k, gen, device)
+        x = torch.randn((m, k), generator=gen, device=device).to(torch.float16)
+        w16 = torch.ops.tokenforge.w4a16_dequant(w.qweight_t, w.scales, w.qzeros, G)
+        ref = x.double() @ w16.double().t()
+        tol = _w4a16_tol(x, w16)
+        entry: dict[str, object] = {"tol": tol}
+        if world == 1:
+            y = ops.w4a16_gemm(x, w.qweight_t, w.scales, w.qzeros, G)
+            err = float((y.double() - ref).abs().max())
+            entry["gemv_err"] = err
+            ok &= err <= tol
+        else:
+            shard = tp.shard_layer(w, "row", rank, world)
+            fused = [tp.linear_shard(x, shard, peers=peers) for _ in range(2)] if peers else []
+            plain = tp.linear_shard(x, shard)
+            if fused:
+                gathered = [torch.empty_like(fused[0]) for _ in range(world)]
+                dist.all_gather(gathered, fused[0])
+                same = all(torch.equal(g, gathered[0]) for g in gathered) and torch.equal(
+                    fused[0], fused[1])
+                err = float((fused[0].double() - ref).abs().max())
+                entry.update({"fused_err": err, "ranks_bit_identical": same})
+                ok &= same and err <= tol
+            err_p = float((plain.double() - ref).abs().max())
+            entry["nccl_err"] = err_p
+            ok &= err_p <= 2 * tol
+        res["layers"][name] = entry  # type: ignore[index]
+        del w16, ref
+    if world > 1:
+        flags = torch.tensor([1 if ok else 0], device=device)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        ok = bool(flags.item())
+        res["peer_error"] = peers.error() if peers else 0
+        ok &= res["peer_error"] == 0
+    res["ok"] = bool(ok)
+    return res
+
+
+def e2e_graph(sweep: DecodeSweep, device: torch.device, steps: int, barrier, world: int) -> dict:  # type: ignore[no-untyped-def]
+    """The sweep end to end through the C ABI, as a user serves it: every step copies the step's
+    activations from pinned host memory to the device, runs the 112 tf_w4a16_linear calls (plus
+    the row-parallel all-reduces) and copies the last output back to pinned host memory; the
+    whole step is one CUDA graph (the calls captured once), replayed once per step."""
+    import torch.distributed as dist
+
+    h_in = [torch.empty_like(x, device="cpu").pin_memory() for x in (sweep.x_h, sweep.x_o, sweep.x_d)]
+    for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
+        hbuf.copy_(x.cpu())
+    y_last = sweep.y[sweep.kinds[-1]]
+    h_out = torch.empty_like(y_last, device="cpu").pin_memory()
+    h2d = sum(h.numel() * h.element_size() for h in h_in)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step() -> None:
+        for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
+            x.copy_(hbuf, non_blocking=True)
+        sweep.step()
+        h_out.copy_(y_last, non_blocking=True)
+
+    g = capture(e2e_step, device)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(device)
+    if barrier:
+        barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    wall_ms = (time.perf_counter() - w0) * 1e3 / steps
+    t = torch.tensor([max(e0.elapsed_time(e1) / steps, wall_ms)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del g
+    return {"ms_per_step": float(t.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "host_matches_device": bool(torch.equal(h_out, y_last.cpu()))}
+
+
+def chain_leg(sweep: DecodeSweep, device: torch.device, steps: int) -> dict | None:
+    """The same sweep as one persistent decode chain (tokenforge_b200.chain.DecodeChain), every op
+    waiting for the one before (as the layers of a real decode step do), timed with CUDA events."""
+    from tokenforge_b200.chain import ChainLinear, DecodeChain
+
+    xs = {"qkv": sweep.x_h, "gate_up": sweep.x_h, "o": sweep.x_o, "down": sweep.x_d}
+    ops_ = [ChainLinear(xs[name], w, sweep.y[name], wait=i > 0)
+            for i, (name, w, _) in enumerate(e for row in sweep.layers for e in row)]
+    try:
+        ch = DecodeChain(ops_)
+    except Exception as e:  # noqa: BLE001 - a shape outside the chain's limits: report, not fail
+        return {"unavailable": str(e)}
+    with ch:
+        for _ in range(3):
+            ch.run()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            ch.run()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / steps
+        err = ch.error()
+    return {"ms_per_step": round(ms, 4), "gbs": round(sweep.bytes_per_step / (ms * 1e-3) / 1e9, 1),
+            "device_error": err, "dependent_ops": True}
+
+
 # ----------------------------------------------------------------------------- block stack (config 4)
 
 
@@ -718,8 +910,8 @@ def main() -> None:
                     help="omit the AWQ repack and RMSNorm+FP8 legs (configs 1 and 2)")
     ap.add_argument("--block-ms", type=str, default="1,64,2048",
                     help="token counts M of the config-4 block-stack leg")
-    ap.add_argument("--block-tp", action="store_true",
-                    help="with --gpus N > 1: also run the config-4 block stack tensor-parallel")
+    ap.add_argument("--skip-chain", action="store_true",
+                    help="omit the persistent decode-chain leg (N = 1)")
     ap.add_argument("--no-fuse-silu", action="store_true",
                     help="block stack: separate SiLU-product and down-projection launches")
     ap.add_argument("--no-fuse-norm", action="store_true",
@@ -813,40 +1005,15 @@ def main() -> None:
         for name in sweep.kinds:
             per_kind[name]["dram_bytes"] = traffic["per_launch"][name]
 
-    # End to end through the C ABI with host buffers: pinned H2D of the step's activations,
-    # 112 eager tf_w4a16_linear calls (plus the all-reduces), D2H of the step's last output.
-    h_in = [torch.empty_like(x, device="cpu").pin_memory() for x in (sweep.x_h, sweep.x_o, sweep.x_d)]
-    for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
-        hbuf.copy_(x.cpu())
-    y_last = sweep.y[sweep.kinds[-1]]
-    h_out = torch.empty_like(y_last, device="cpu").pin_memory()
-    h2d = sum(h.numel() * h.element_size() for h in h_in)
-    d2h = h_out.numel() * h_out.element_size()
-
-    def e2e_step() -> None:
-        for hbuf, x in zip(h_in, (sweep.x_h, sweep.x_o, sweep.x_d)):
-            x.copy_(hbuf, non_blocking=True)
-        sweep.step()
-        h_out.copy_(y_last, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize(device)
-    if barrier:
-        barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize(device)
-    wall_ms = (time.perf_counter() - w0) * 1e3 / args.steps
-    e2e_ms = torch.tensor([max(e0.elapsed_time(e1) / args.steps, wall_ms)], device=device,
-                          dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = total_bytes / (float(e2e_ms.item()) * 1e-3) / 1e9
+    # End to end through the C ABI with host buffers (pinned H2D of the step's activations, the
+    # calls, D2H of the last output), captured once as a graph and replayed per step.
+    e2e = e2e_graph(sweep, device, args.steps, barrier, world)
+    e2e_value = total_bytes / (e2e["ms_per_step"] * 1e-3) / 1e9
+    # Correctness of the timed paths at this N (fused all-reduce across ranks at N > 1).
+    parity = decode_parity(device, rank, world, peers, min(args.m, 8))
+    chain = None
+    if world == 1 and full and not args.skip_chain and args.m <= 8:
+        chain = chain_leg(sweep, device, args.steps)
 
     gemm = None
     if world == 1 and not args.skip_gemm:
@@ -858,7 +1025,7 @@ def main() -> None:
         extra["repack"] = repack_metric(device, max(3, args.steps // 2), pk)
         extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None
-    if full and not args.skip_block and (world == 1 or args.block_tp):
+    if full and not args.skip_block:
         block = block_metric(sweep, device, tuple(int(v) for v in args.block_ms.split(",")),
                              max(3, args.steps // 2), fuse_norm=not args.no_fuse_norm,
                              rank=rank, world=world, peers=peers, barrier=barrier,
@@ -866,6 +1033,13 @@ def main() -> None:
     cpu = None
     if rank == 0 and world == 1 and full and not args.skip_cpu:
         cpu = cpu_baseline(args.m, min_seconds=10.0)
+        cpu["cpu_model"] = cpu_model()
+        aux_cpu = cpu_aux_baselines()
+        if gemm is not None:
+            gemm["cpu_baseline"] = aux_cpu["gemm"]
+        for leg in ("repack", "rmsnorm_fp8"):
+            if leg in extra:
+                extra[leg]["cpu_baseline"] = aux_cpu[leg]
 
     if rank == 0:
         line = {
@@ -905,9 +1079,15 @@ def main() -> None:
                            "w4a16_tc_kernel (tcgen05 GEMM)"),
                 "per_layer": per_kind,
             },
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(float(e2e_ms.item()), 4),
-                    "path": "tf_w4a16_linear via ctypes, eager, pinned host buffers"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                    "ms_per_step": round(e2e["ms_per_step"], 4),
+                    "host_matches_device": e2e["host_matches_device"],
+                    "path": "tf_w4a16_linear C ABI calls with pinned H2D / D2H copies, the step "
+                            "captured as one CUDA graph and replayed per step"},
+            "parity": parity,
+            "chain": chain,
             "gpu_launches": sweep.launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
@@ -917,6 +1097,8 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     del graph
+    if not parity["ok"]:
+        print(f"parity check failed: {json.dumps(parity)}", file=sys.stderr)
     if peers is not None:
         if peers.error():
             print("peer all-reduce: a wait timed out", file=sys.stderr)
@@ -924,6 +1106,8 @@ def main() -> None:
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if not parity["ok"]:
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -105,19 +105,25 @@ __device__ __forceinline__ void mma_16816_zc(float (&d)[4], const uint32_t (&a)[
 
 // The four rows' zero points of a group-size-128 block as fp16x2 broadcasts: z0[j] = (1024 + z_j)
 // twice and z1[j] = (64 + z_j) twice. The rows' zero points sit in nibbles {0, 4, 1, 5} of the
-// qzeros word shifted by nib[0] (0 or 8): one LOP3 per row pair gives (1024 + z_a, 1024 + z_b),
-// a byte permute broadcasts each row's value, and 1024 + z - 960 = 64 + z exactly.
+// qzeros word shifted by nib[0] (0 or 8): one LOP3 per row pair places them in the mantissa of
+// 0x6400 (1024 + z, unit steps in bits 0-3) or, four bits higher, of 0x5400 (64 + z, unit steps
+// in bits 4-7), and a byte permute broadcasts each row's value to both halves. Integer and
+// permute instructions only, so the fp16 pipe is left to the per-weight dequant.
 __device__ __forceinline__ void zero_points(uint32_t (&z0)[4], uint32_t (&z1)[4], uint32_t zword,
                                             int nib0) {
   const uint32_t zs = zword >> nib0;
-  const uint32_t a = lop_mask_or(zs, 0x000F000Fu, 0x64006400u);
-  const uint32_t b = lop_mask_or(zs >> 4, 0x000F000Fu, 0x64006400u);
+  const uint32_t a = lop_mask_or(zs, 0x000F000Fu, 0x64006400u);        // rows 0, 1: 1024 + z
+  const uint32_t b = lop_mask_or(zs >> 4, 0x000F000Fu, 0x64006400u);   // rows 2, 3: 1024 + z
+  const uint32_t a1 = lop_mask_or(zs << 4, 0x00F000F0u, 0x54005400u);  // rows 0, 1: 64 + z
+  const uint32_t b1 = lop_mask_or(zs, 0x00F000F0u, 0x54005400u);       // rows 2, 3: 64 + z
   z0[0] = __byte_perm(a, a, 0x1010u);
   z0[1] = __byte_perm(a, a, 0x3232u);
   z0[2] = __byte_perm(b, b, 0x1010u);
   z0[3] = __byte_perm(b, b, 0x3232u);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) z1[j] = hsub2_rn(z0[j], 0x63806380u);  // fp16 960
+  z1[0] = __byte_perm(a1, a1, 0x1010u);
+  z1[1] = __byte_perm(a1, a1, 0x3232u);
+  z1[2] = __byte_perm(b1, b1, 0x1010u);
+  z1[3] = __byte_perm(b1, b1, 0x3232u);
 }
 
 // The lane's 4 x 16 dequantized fp16x2 pairs of one word column i of a group-size-128 block, in

@@ -52,7 +52,7 @@ namespace {
 
 constexpr int kWarps = 16;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kRing = 2;                      // chunk slots per warp
+constexpr int kRing = 3;                      // chunk slots per warp (two in flight while one is read)
 constexpr int kChunkK = 256;                  // K values per chunk
 constexpr int kTileRows = 32;                 // weight rows per row tile
 constexpr int kWBytes = kTileRows * 128;      // packed weights of a chunk: 32 rows x 128 bytes
@@ -72,14 +72,16 @@ constexpr unsigned long long kChainWaitNs = 2000000000ull;
 constexpr int kOffW = 0;
 constexpr int kOffSZ = kOffW + kWarps * kRing * kWBytes;
 constexpr int kOffBar = kOffSZ + kWarps * kRing * kSZBytes;
-constexpr int kOffRed = kOffBar + kWarps * kRing * 8;
-constexpr int kOffMisc = kOffRed + kWarps * kRedFloats * 4;
-constexpr int kOffX = kOffMisc + 64;
+constexpr int kOffMisc = kOffBar + kWarps * kRing * 8;  // epoch, last-arrival flags of 16 tiles
+// The staged activations and the cross-warp reduction buffer share one region: a unit's partials
+// are written only after every warp has finished reading its activations.
+constexpr int kOffX = kOffMisc + 128;
+constexpr int kRedBytes = kWarps * kRedFloats * 4;
 constexpr int kSmemCap = 227 * 1024;
 constexpr int kAlignSlack = 1024;
 static_assert(kOffW % 1024 == 0 && kWBytes % 1024 == 0, "128-byte-swizzled boxes need 1 KB alignment");
 static_assert(kOffSZ % 128 == 0 && kSZBytes % 128 == 0, "TMA destinations need 128-byte alignment");
-static_assert(kOffBar % 8 == 0 && kOffRed % 16 == 0 && kOffX % 16 == 0, "shared-memory alignment");
+static_assert(kOffBar % 8 == 0 && kOffX % 16 == 0, "shared-memory alignment");
 
 // Error codes recorded in the chain's error word (first one wins).
 constexpr uint32_t kErrDepWait = 0x201;    // an op's dependency counter did not complete in time
@@ -157,30 +159,47 @@ __device__ __forceinline__ float ld_cg_f32(const float* p) {
   return v;
 }
 
-// The sequence of (unit, chunk) one warp consumes, walked ahead by the TMA issue side.
+// The sequence of (unit, chunk) one warp consumes, walked ahead by the TMA issue side. The
+// current unit's fields are cached, so stepping within a unit reads no memory.
 struct ChunkWalk {
   int u, u_end;
-  int c;  // next chunk of unit u for this warp (-1: unit not entered yet)
-  int op, tile, step;
+  int c, c1, step;  // next chunk of unit u, end of its range, this warp's stride
+  int op, tile;
+  bool live;
 };
 
-// Positions the walk on this warp's next chunk at or after its current position; false at end.
-__device__ __forceinline__ bool walk_seek(ChunkWalk& w, const ChainParams& p, int warp) {
-  while (w.u < w.u_end) {
+// Moves to the first unit at or after w.u in which this warp has a chunk; false at the end.
+// Entering an op's first unit prefetches the tensor maps of the op after it, so the descriptor
+// is on chip before its first copy.
+__device__ __forceinline__ bool walk_enter(ChunkWalk& w, const ChainParams& p, int warp, int lane) {
+  for (; w.u < w.u_end; ++w.u) {
     const ChainUnitDev U = p.units[w.u];
     const int R = U.rtiles;
     const int tile = U.tile0 + warp % R;
-    if (w.c < 0) w.c = U.c0 + warp / R;
-    if (tile < p.ops[U.op].tiles && w.c < U.c1) {
+    const int c = U.c0 + warp / R;
+    if (tile < p.ops[U.op].tiles && c < U.c1) {
+      if (lane == 0 && U.op != w.op && U.op + 1 < p.n_ops) {
+        const ChainOpDev* nx = p.ops + U.op + 1;
+        prefetch_tmap(&nx->mw);
+        prefetch_tmap(&nx->ms);
+        prefetch_tmap(&nx->mz);
+      }
+      w.c = c;
+      w.c1 = U.c1;
+      w.step = kWarps / R;
       w.op = U.op;
       w.tile = tile;
-      w.step = kWarps / R;
       return true;
     }
-    ++w.u;
-    w.c = -1;
   }
   return false;
+}
+
+__device__ __forceinline__ void walk_next(ChunkWalk& w, const ChainParams& p, int warp, int lane) {
+  w.c += w.step;
+  if (w.c < w.c1) return;
+  ++w.u;
+  w.live = walk_enter(w, p, warp, lane);
 }
 
 // Lane 0: the three TMA boxes of one chunk into ring slot `slot` of warp `warp`. `reuse`: the
@@ -199,15 +218,13 @@ __device__ __forceinline__ void issue_chunk(const ChainParams& p, uint8_t* smem,
 }
 
 // Block b (0 or 1) of a chunk in the ring as this lane's GSlot: rows 4q..4q+3, 16 bytes each at
-// logical 16-byte column 4b + c of the 128-byte swizzled rows (physical column = logical ^ row % 8).
-__device__ __forceinline__ void ring_block(GSlot& s, const uint8_t* w, const uint8_t* sz, int b,
-                                           int q, int c) {
+// logical 16-byte column 4b + c of the 128-byte swizzled rows; physical column = logical ^ (row
+// % 8) = 4 (b ^ (q % 2)) + (c ^ j) for row 4q + j. loff[j] = row * 128 + 16 (c ^ j) and
+// boff = 64 (b ^ (q % 2)) are per-lane constants.
+__device__ __forceinline__ void ring_block(GSlot& s, const uint8_t* w, const uint8_t* sz,
+                                           const uint32_t (&loff)[4], uint32_t boff, int b, int q) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int row = 4 * q + j;
-    const int phys = (4 * b + c) ^ (row & 7);
-    s.w[j] = *reinterpret_cast<const uint4*>(w + row * 128 + phys * 16);
-  }
+  for (int j = 0; j < 4; ++j) s.w[j] = *reinterpret_cast<const uint4*>(w + loff[j] + boff);
   s.s = *reinterpret_cast<const uint2*>(sz + b * 64 + q * 8);
   s.z = *reinterpret_cast<const uint32_t*>(sz + kZOffInSZ + b * 16 + (q >> 1) * 4);
 }
@@ -235,27 +252,22 @@ __device__ __forceinline__ void stage_x(const ChainParams& p, const ChainOpDev& 
   asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// Writes one row tile's result: v[t][r] is row 4q + 2t + (r >> 1), token 2c + (r & 1).
-__device__ __forceinline__ void write_tile(const ChainOpDev& o, int M, int tile, const float (&v)[2][4],
-                                           int q, int c) {
-#pragma unroll
-  for (int t = 0; t < 2; ++t)
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int n = tile * kTileRows + 4 * q + 2 * t + (r >> 1);
-      const int m = 2 * c + (r & 1);
-      if (m >= M || n >= o.n) continue;
-      float out = v[t][r];
-      if (o.bias) out += __half2float(__ldg(o.bias + n));
-      o.y[static_cast<int64_t>(m) * o.ldy + n] = __float2half_rn(out);
-    }
+// Fragment value f (t * 4 + r) of lane ln in a warp's 32-row tile: row 4 (ln / 4) + 2t + r / 2,
+// token 2 (ln % 4) + r % 2 (the m16n8 accumulator layout of the two 16-row MMA tiles).
+__device__ __forceinline__ void write_value(const ChainOpDev& o, int M, int tile, int f, int ln,
+                                            float v) {
+  const int n = tile * kTileRows + 4 * (ln >> 2) + 2 * (f >> 2) + ((f & 3) >> 1);
+  const int m = 2 * (ln & 3) + (f & 1);
+  if (m >= M || n >= o.n) return;
+  if (o.bias) v += __half2float(__ldg(o.bias + n));
+  o.y[static_cast<int64_t>(m) * o.ldy + n] = __float2half_rn(v);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  float* red = reinterpret_cast<float*>(smem + kOffRed);
+  float* red = reinterpret_cast<float*>(smem + kOffX);  // aliases xs (see kOffX)
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   __half* xs = reinterpret_cast<__half*>(smem + kOffX);
 
@@ -273,21 +285,29 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
   const uint32_t done_target = (epoch + 1u) * gridDim.x;
 
   const int u_begin = p.cta_units[blockIdx.x], u_end = p.cta_units[blockIdx.x + 1];
+  uint8_t* ring_w = smem + kOffW + warp * kRing * kWBytes;
+  uint8_t* ring_sz = smem + kOffSZ + warp * kRing * kSZBytes;
+  uint32_t loff[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) loff[j] = (4 * q + j) * 128 + 16 * (c ^ j);
+  const uint32_t boff0 = 64u * (q & 1), boff1 = 64u - boff0;
 
   // TMA issue side of this warp: `issued` chunks so far, walking ahead of consumption.
-  ChunkWalk walk{u_begin, u_end, -1, 0, 0, 0};
+  ChunkWalk walk;
+  walk.u = u_begin;
+  walk.u_end = u_end;
+  walk.op = -1;
+  walk.live = walk_enter(walk, p, warp, lane);
   int issued = 0;
-  bool walk_live = walk_seek(walk, p, warp);
+  // Keeps kRing chunks in flight: slot (issued % kRing) last held chunk issued - kRing, which the
+  // warp has finished reading (consumed > issued - kRing).
   auto top_up = [&](int consumed) {
-    // Keep kRing chunks in flight: slot (issued % kRing) last held chunk issued - kRing, which
-    // the warp finished reading (consumed > issued - kRing).
     __syncwarp();
-    while (walk_live && issued < consumed + kRing) {
+    while (walk.live && issued < consumed + kRing) {
       if (lane == 0)
         issue_chunk(p, smem, warp, issued % kRing, walk.op, walk.tile, walk.c, issued >= kRing);
       ++issued;
-      walk.c += walk.step;
-      walk_live = walk_seek(walk, p, warp);
+      walk_next(walk, p, warp, lane);
     }
   };
   top_up(0);
@@ -325,14 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
       }
       passed = U.op;
     }
-    __syncthreads();  // dependency passed; the previous unit's reduction buffer is free
+    __syncthreads();  // dependency passed; the previous unit's reads of xs and red are done
     stage_x(p, o, xs, U.c0, U.c1);
     __syncthreads();
 
     const int R = U.rtiles, P = kWarps / R;
     const int tile = U.tile0 + warp % R;
     const int j = warp / R;
-    const bool tile_ok = tile < o.tiles;
     if (U.flags & kFirst) {
 #pragma unroll
       for (int t = 0; t < 2; ++t)
@@ -344,71 +363,70 @@ __global__ void __launch_bounds__(kThreads, 1) w4a16_chain_kernel(const ChainPar
     L.kb0 = 2 * U.c0;
     L.nib[0] = (q & 1) ? 8 : 0;  // rows 4q..4q+3: zero points in nibbles {0,4,1,5} or {2,6,3,7}
     L.xs = xs4 + (min(q, p.M - 1) * p.x_stride + 32 * c) / 8;
-    if (tile_ok) {
+    if (tile < o.tiles) {
       for (int ch = U.c0 + j; ch < U.c1; ch += P) {
         top_up(consumed);
         const int slot = consumed % kRing;
         if (!chunk_wait(&bars[warp * kRing + slot], (consumed / kRing) & 1u, p.ctl)) timed_out = true;
-        const uint8_t* wt = smem + kOffW + (warp * kRing + slot) * kWBytes;
-        const uint8_t* sz = smem + kOffSZ + (warp * kRing + slot) * kSZBytes;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          GSlot s;
-          ring_block(s, wt, sz, b, q, c);
-          gcompute_w16(acc, s, 2 * ch + b, L);
-        }
+        const uint8_t* wt = ring_w + slot * kWBytes;
+        const uint8_t* sz = ring_sz + slot * kSZBytes;
+        GSlot s0, s1;
+        ring_block(s0, wt, sz, loff, boff0, 0, q);
+        ring_block(s1, wt, sz, loff, boff1, 1, q);
+        gcompute_w16(acc, s0, 2 * ch, L);
+        gcompute_w16(acc, s1, 2 * ch + 1, L);
         ++consumed;
       }
     }
     if (!(U.flags & kLast)) continue;
 
-    // Reduce the P warps of each row tile in warp order, then write (or hand the piece over).
+    // Reduce: every warp publishes its tile's partial (over the activations, which every warp
+    // has finished reading); then all threads of the CTA sum the P warps of each row tile in
+    // warp order, one fragment value each, and write it.
+    __syncthreads();
     float* mine = red + warp * kRedFloats;
 #pragma unroll
     for (int t = 0; t < 2; ++t)
 #pragma unroll
       for (int r = 0; r < 4; ++r) mine[(t * 4 + r) * 32 + lane] = acc[t][0][r] + acc[t][1][r];
     __syncthreads();
-    if (j != 0 || !tile_ok) continue;
-    float v[2][4];
+    const int nvals = R * kRedFloats;
+    const bool split = (U.flags & kSplit) != 0;
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float a = 0.f;
-        for (int jj = 0; jj < P; ++jj) a += red[(warp + jj * R) * kRedFloats + (t * 4 + r) * 32 + lane];
-        v[t][r] = a;
+    for (int i = 0; i < kRedFloats * kWarps / kThreads; ++i) {  // R * 256 values, <= 8 per thread
+      const int v = tid + i * kThreads;
+      if (v >= nvals) continue;
+      const int r_in = v / kRedFloats, fl = v % kRedFloats;
+      float a = 0.f;
+      for (int jj = 0; jj < P; ++jj) a += red[(r_in + jj * R) * kRedFloats + fl];
+      if (!split) {
+        if (U.tile0 + r_in < o.tiles) write_value(o, p.M, U.tile0 + r_in, fl >> 5, fl & 31, a);
+      } else {
+        p.partials[static_cast<int64_t>(U.slot + U.piece * R + r_in) * kRedFloats + fl] = a;
       }
-    if (!(U.flags & kSplit)) {
-      write_tile(o, p.M, tile, v, q, c);
-      continue;
     }
-    // A piece of a tile split across CTAs: publish it; the last CTA to arrive sums all pieces.
-    const int r_in = warp % R;
-    float* part = p.partials + static_cast<int64_t>(U.slot + U.piece * R + r_in) * kRedFloats;
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) part[(t * 4 + r) * 32 + lane] = v[t][r];
+    if (!split) continue;
+    // A piece of tiles split across CTAs: the last CTA to publish its piece of a tile sums all
+    // pieces in piece order and writes the tile.
     __threadfence();
-    __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atom_acq_rel_gpu_add(p.counters + U.counter + r_in, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1u != (epoch + 1u) * U.pieces) continue;
-    __syncwarp();  // lane 0's acquire orders the other lanes' reads of the pieces
+    __syncthreads();
+    if (tid < R) {
+      const uint32_t old = atom_acq_rel_gpu_add(p.counters + U.counter + tid, 1u);
+      misc[8 + tid] = (old + 1u == (epoch + 1u) * U.pieces) ? 1u : 0u;
+    }
+    __syncthreads();
     __threadfence();
-    const float* base = p.partials + static_cast<int64_t>(U.slot + r_in) * kRedFloats;
 #pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float a = 0.f;
-        for (int pc = 0; pc < U.pieces; ++pc)
-          a += ld_cg_f32(base + static_cast<int64_t>(pc) * R * kRedFloats + (t * 4 + r) * 32 + lane);
-        v[t][r] = a;
-      }
-    write_tile(o, p.M, tile, v, q, c);
+    for (int i = 0; i < kRedFloats * kWarps / kThreads; ++i) {
+      const int v = tid + i * kThreads;
+      if (v >= nvals) continue;
+      const int r_in = v / kRedFloats, fl = v % kRedFloats;
+      if (!misc[8 + r_in] || U.tile0 + r_in >= o.tiles) continue;
+      float a = 0.f;
+      for (int pc = 0; pc < U.pieces; ++pc)
+        a += ld_cg_f32(p.partials + static_cast<int64_t>(U.slot + pc * R + r_in) * kRedFloats + fl);
+      write_value(o, p.M, U.tile0 + r_in, fl >> 5, fl & 31, a);
+    }
   }
 
   // Publish the remaining arrivals, drain this warp's copies if a wait gave up, and let the last
@@ -449,7 +467,7 @@ int ceil_div(int a, int b) { return (a + b - 1) / b; }
 // the shared memory left after the rings, barriers and reduction buffer.
 int max_unit_chunks(int M) {
   const int budget = kSmemCap - kAlignSlack - kOffX;
-  return (budget / (2 * M) - 8) / kChunkK;
+  return std::min((budget / (2 * M) - 8) / kChunkK, 65535);
 }
 
 void emit_piece(ChainPlan& pl, int cta, int op, int tile0, int R, int c0, int c1, int piece,
@@ -705,7 +723,8 @@ int tf_decode_chain_create(const TfChainOp* ops, int32_t n_ops, int64_t M, int32
   ch->device = dev;
   ch->grid = sms;
   const int x_stride = pl.max_chunks * kChunkK + 8;
-  ch->smem = static_cast<size_t>(kAlignSlack + kOffX) + static_cast<size_t>(M) * x_stride * 2;
+  ch->smem = static_cast<size_t>(kAlignSlack + kOffX) +
+             std::max(static_cast<size_t>(M) * x_stride * 2, static_cast<size_t>(kRedBytes));
   e = cudaMalloc(&ch->mem, total);
   char* base = static_cast<char*>(ch->mem);
   if (e == cudaSuccess)
