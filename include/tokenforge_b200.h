@@ -65,11 +65,12 @@ TF_API int tf_last_cuda_error(void);
 TF_API int tf_abi_version(void);
 
 /* Process-wide launch flags.
- * TF_LAUNCH_PDL: W4A16 linear kernels are launched with programmatic dependent launch and
- *   start streaming their weights before the preceding kernel on the stream has finished
- *   (activations are read, and outputs written, only after it has). Set it only when no
- *   kernel enqueued directly before a W4A16 call on the same stream writes that call's
- *   qweight_t, scales or qzeros. Off by default. */
+ * TF_LAUNCH_PDL: W4A16 linear kernels and the RMSNorm + FP8 quantizer are launched with
+ *   programmatic dependent launch and start reading their weights (qweight_t, scales, qzeros;
+ *   the RMSNorm weight) before the preceding kernel on the stream has finished (activations
+ *   are read, and outputs written, only after it has). Set it only when no kernel enqueued
+ *   directly before such a call on the same stream writes that call's weights. Off by
+ *   default. */
 #define TF_LAUNCH_PDL 1u
 TF_API void tf_set_launch_flags(uint32_t flags);
 TF_API uint32_t tf_get_launch_flags(void);
@@ -289,8 +290,23 @@ TF_API int tf_rmsnorm_fp8_quant(const uint16_t* x, int64_t T, int64_t H, int64_t
  * (tests/numerics/test_rmsnorm_fp8.py:22-27). */
 TF_API int tf_cast_e4m3(const float* in, int64_t n, uint8_t* out, void* stream);
 
-/* Device-side status word written by kernels whose waits are bounded (the tcgen05 GEMM):
- * 0 = no error. Reading it synchronises the current device; resetting writes 0. */
+/* The quantization step of tf_rmsnorm_fp8_quant on its own, for activations already
+ * normalised: q[r, c] = e4m3_rne_satfinite(clamp(y[r, c] / scale_r, -448, 448)) with the IEEE
+ * fp32 division's rounding (reference tokenforge/kernels/reference.py:47-49).
+ *   scale != NULL: scale_r = scale[r * scale_stride] (scale_stride 0: one static scale; 1: per
+ *                  row); scale_out is not written;
+ *   scale == NULL: dynamic, scale_r = max(amax_c |y[r, c]| / 448, 1 / (448 * 512)), written to
+ *                  scale_out[r].
+ * y: fp16 [R, C] row stride ldy; q: e4m3 [R, C] contiguous. No reference counterpart as a
+ * separate op. */
+TF_API int tf_e4m3_quant_rows(const uint16_t* y, int64_t R, int64_t C, int64_t ldy,
+                              const float* scale, int64_t scale_stride, uint8_t* q,
+                              float* scale_out, void* stream);
+
+/* Device-side status word written by kernels whose waits are bounded: 0 = no error; 0x1xx the
+ * tcgen05 GEMM (a pipeline wait gave up), 0x301 the RMSNorm + FP8 streaming kernel (a row's
+ * bulk copy did not complete in time). Reading it synchronises the current device; resetting
+ * writes 0. */
 TF_API int tf_device_error(int* out_code);
 TF_API int tf_reset_device_error(void);
 

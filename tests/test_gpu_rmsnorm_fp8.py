@@ -3,6 +3,7 @@ tests/numerics/test_rmsnorm_fp8.py, plus the BASELINE config-1 shapes (outlier c
 
 from __future__ import annotations
 
+import ctypes
 from pathlib import Path
 
 import numpy as np
@@ -194,3 +195,141 @@ def test_many_rows(t: int, h: int, device: torch.device) -> None:
     q, _ = rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS, static.to(device))
     q_ref, _ = oracle.rmsnorm_fp8(x, w, EPS, static)
     assert torch.equal(_codes(q), q_ref.to(torch.int16))
+
+
+def _ieee_quant(y: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """e4m3(clamp(y / scale)) with torch's IEEE fp32 division (tensor by tensor: torch divides
+    by a Python scalar through its reciprocal) and its float8_e4m3fn cast."""
+    v = (y.float() / scale.reshape(-1, 1)).clamp(-FP8_MAX, FP8_MAX)
+    return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def _all_fp16(device: torch.device) -> torch.Tensor:
+    return torch.arange(-32768, 32768, dtype=torch.int32, device=device).to(torch.int16).view(
+        torch.float16)
+
+
+def test_quant_division_matches_ieee_for_every_dynamic_scale(device: torch.device) -> None:
+    """The quantizer divides by the row scale with FMAs (a reciprocal and residual corrections),
+    not an IEEE division per element; dynamic scales take one correction step, which is exact
+    for them only as a fact about this finite set. Exhaustive check of that fact through the
+    dynamic quantizer itself: for every positive finite fp16 amax h, a row holding h and every
+    fp16 value y with |y| <= h (the only quotients the dynamic rule can form), codes bit-exact
+    with IEEE division and the float8 cast, and the scale max(h / 448, 1 / (448 * 512)) exact;
+    NaN elements give NaN codes."""
+    from tokenforge_b200.ops import e4m3_quant_rows
+
+    ys = _all_fp16(device)
+    nan_cols = torch.isnan(ys)
+    amaxes = torch.arange(1, 0x7C00, dtype=torch.int32, device=device).to(torch.int16).view(
+        torch.float16)
+    for h in amaxes.split(512):
+        y = torch.where(ys.abs().unsqueeze(0) <= h.unsqueeze(1), ys.unsqueeze(0), h.unsqueeze(1))
+        y = torch.where(nan_cols.unsqueeze(0), ys.unsqueeze(0), y).contiguous()
+        got, scale = e4m3_quant_rows(y)
+        hf = h.float()
+        want_scale = torch.clamp(hf / torch.full_like(hf, FP8_MAX),
+                                 min=1.0 / (FP8_MAX * 512)).unsqueeze(1)
+        assert torch.equal(scale, want_scale)
+        got = got.view(torch.uint8)
+        want = _ieee_quant(y, want_scale)
+        assert torch.equal(got[:, ~nan_cols], want[:, ~nan_cols])
+        assert bool(((got[:, nan_cols] & 0x7F) == 0x7F).all())
+    # the scalar path (C not a multiple of 8), and a row with an Inf (IEEE-division path)
+    y = ys[: 3 * 1001].reshape(3, 1001).clone()
+    y[1, 5] = float("inf")
+    got, scale = e4m3_quant_rows(y)
+    fin = ~torch.isnan(y)
+    assert torch.equal(got.view(torch.uint8)[fin], _ieee_quant(y, scale)[fin])
+
+
+def test_quant_division_matches_ieee_for_static_scales(device: torch.device) -> None:
+    """Static scales take two correction steps: scales across the FMA path's range [2^-60,
+    2^60] (log-uniform), its edges, and outside it (IEEE-division path: tiny, subnormal and huge
+    scales), against every fp16 value, bit-exact; also the scalar path (C not a multiple of 8)
+    and one scale for all rows."""
+    from tokenforge_b200.ops import e4m3_quant_rows
+
+    gen = torch.Generator().manual_seed(4)
+    logs = torch.rand(2048, generator=gen, dtype=torch.float64) * 120 - 60
+    edges = torch.tensor([2.0**-60, 2.0**60, 2.0**-61, 2.0**61, 1e-30, 1e-40, 3e38, 1.0, 448.0],
+                         dtype=torch.float64)
+    scales = torch.cat([torch.exp2(logs), edges]).to(torch.float32).to(device)
+    ys = _all_fp16(device)
+    nan = torch.isnan(ys)
+    for s in scales.split(512):
+        y = ys.expand(s.numel(), -1).contiguous()
+        got = e4m3_quant_rows(y, s)[0].view(torch.uint8)
+        want = _ieee_quant(y, s)
+        assert torch.equal(got[:, ~nan], want[:, ~nan])
+    one = scales[:3]
+    y = ys[: 3 * 1001].reshape(3, 1001)
+    fin = ~torch.isnan(y)
+    got = e4m3_quant_rows(y, one)[0].view(torch.uint8)
+    assert torch.equal(got[fin], _ieee_quant(y, one)[fin])
+    static = e4m3_quant_rows(y, one[1:2])[0].view(torch.uint8)
+    assert torch.equal(static[fin], _ieee_quant(y, one[1:2].expand(3))[fin])
+
+
+@pytest.mark.parametrize("h", [10000, 16384, 40000])
+@pytest.mark.parametrize("t", [3, 1030])
+def test_long_rows_bit_exact(t: int, h: int, device: torch.device) -> None:
+    """Rows past one vector per thread (H > 8192: two or four vectors per thread) and past the
+    CTA-per-row kernel's reach (H = 40000: the generic path), bit-exact with the oracle."""
+    x, w = _inputs(t, h, seed=h + t)
+    q, s = rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS)
+    q_ref, s_ref = oracle.rmsnorm_fp8(x, w, EPS)
+    assert torch.equal(_codes(q), q_ref.to(torch.int16))
+    assert torch.equal(s.cpu(), s_ref)
+
+
+@pytest.mark.parametrize("t", [2, 1100])
+def test_signed_zeros_tiny_values_and_infinite_products(t: int, device: torch.device) -> None:
+    """The FMA division's edge cases, bit-exact with the oracle: +-0 and fp16 subnormal
+    activations (the sign of zero), a weight large enough that some products y overflow to Inf
+    (dynamic: an Inf row scale; static: the IEEE-division fallback of the threads that hold an
+    Inf), and static scales outside the FMA path's range."""
+    h = 3584
+    x, w = _inputs(t, h, seed=99 + t)
+    x[:, :64] = 0.0
+    x[:, 1:64:2] = -0.0
+    x[:, 64:128] = torch.tensor(6e-8, dtype=torch.float16) * torch.arange(-32, 32)
+    x[0, 300] = 100.0
+    w[300] = 60000.0
+    for static in (None, 1e-30, 2.0**61, 0.05):
+        sc = None if static is None else torch.tensor([static], dtype=torch.float32)
+        q, s = rmsnorm_fp8_quant_2d(x.to(device), w.to(device), EPS,
+                                    None if sc is None else sc.to(device))
+        q_ref, s_ref = oracle.rmsnorm_fp8(x, w, EPS, sc)
+        ref_nan = torch.isnan(q_ref.view(torch.float8_e4m3fn).float())
+        assert torch.equal(torch.isnan(q.cpu().float()), ref_nan), f"static scale {static}"
+        assert torch.equal(_codes(q)[~ref_nan], q_ref.to(torch.int16)[~ref_nan]), static
+        assert torch.equal(s.cpu(), s_ref)
+        if static is None:
+            assert float(s_ref[0, 0]) == float("inf"), "row 0 must hold an Inf product"
+
+
+@pytest.mark.parametrize("h", [1032, 2048, 3000, 3584, 4096])
+@pytest.mark.parametrize("t", [600, 5001])
+def test_streaming_rows_bit_exact(t: int, h: int, device: torch.device) -> None:
+    """Many rows of 1024 to 4096 elements go to the persistent streaming kernel (rows copied
+    into per-warp shared-memory rings); dynamic and static scales, a row-strided view, and row
+    counts that leave warps of the grid with different numbers of rows. The device status word
+    stays clear (no bounded wait gave up)."""
+    from tokenforge_b200 import _lib
+
+    x, w = _inputs(t, h, seed=7 * h + t)
+    wide = torch.zeros((t, h + 24), dtype=torch.float16)
+    wide[:, :h] = x
+    xd = wide.to(device)[:, :h]
+    q, s = rmsnorm_fp8_quant_2d(xd, w.to(device), EPS)
+    q_ref, s_ref = oracle.rmsnorm_fp8(x, w, EPS)
+    assert torch.equal(_codes(q), q_ref.to(torch.int16))
+    assert torch.equal(s.cpu(), s_ref)
+    sc = torch.tensor([0.011], dtype=torch.float32)
+    q, _ = rmsnorm_fp8_quant_2d(xd, w.to(device), EPS, sc.to(device))
+    q_ref, _ = oracle.rmsnorm_fp8(x, w, EPS, sc)
+    assert torch.equal(_codes(q), q_ref.to(torch.int16))
+    code = ctypes.c_int(-1)
+    _lib.check("tf_device_error", _lib.lib().tf_device_error(ctypes.byref(code)))
+    assert code.value == 0

@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tf_launch_plan": (ctypes.c_int, [_I64, _I64, _I64, _I32, _P]),
     "tf_rmsnorm_fp8_quant": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _F32, _P, _P, _P, _P]),
     "tf_cast_e4m3": (ctypes.c_int, [_P, _I64, _P, _P]),
+    "tf_e4m3_quant_rows": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _P]),
     "tf_device_error": (ctypes.c_int, [_P]),
     "tf_reset_device_error": (ctypes.c_int, []),
     "tf_decode_chain_create": (ctypes.c_int, [_P, _I32, _I64, _I32, _P]),

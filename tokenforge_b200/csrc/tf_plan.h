@@ -34,6 +34,10 @@ int plan_linear(int64_t M, int64_t N, int64_t K, int group_size, LinearPlan* pla
 // Process-wide launch flags (tf_set_launch_flags).
 uint32_t launch_flags();
 
+// Status word of the RMSNorm streaming kernel's bounded waits (rmsnorm_fp8.cu).
+int rms_device_error(int* code);
+int rms_reset_device_error();
+
 struct LinearArgs {
   const uint16_t* x;
   int64_t M, K, ldx;

@@ -649,6 +649,7 @@ int launch_tc_gemm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t strea
 
 }  // namespace tfb
 
+// The GEMM's status word first (0x1xx codes), else the RMSNorm streaming kernel's (0x3xx).
 extern "C" int tf_device_error(int* out_code) {
   if (!out_code) return TF_ERR_INVALID_ARG;
   const cudaError_t e = cudaMemcpyFromSymbol(out_code, tfb::g_device_error, sizeof(int));
@@ -656,7 +657,7 @@ extern "C" int tf_device_error(int* out_code) {
     tfb::last_cuda_error() = static_cast<int>(e);
     return TF_ERR_CUDA;
   }
-  return TF_OK;
+  return *out_code != 0 ? TF_OK : tfb::rms_device_error(out_code);
 }
 
 extern "C" int tf_reset_device_error(void) {
@@ -666,5 +667,5 @@ extern "C" int tf_reset_device_error(void) {
     tfb::last_cuda_error() = static_cast<int>(e);
     return TF_ERR_CUDA;
   }
-  return TF_OK;
+  return tfb::rms_reset_device_error();
 }

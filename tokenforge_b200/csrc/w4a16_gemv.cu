@@ -373,10 +373,24 @@ __device__ __forceinline__ void stage_silu(const GemvParams& p, uint4* xs_smem, 
   }
 }
 
+// Replaces the staged -y values of one row by the fp16 values of their e4m3 codes.
+template <int kPath>
+__device__ __forceinline__ void quant_staged(uint4* row, int nvec, int tid, int nt, const Fp8Div& d) {
+  for (int j = tid; j < nvec; j += nt) {
+    const uint2 c = quant_vec<kPath>(row[j], d);
+    uint4 v;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(v.x) : "h"(static_cast<uint16_t>(c.x)));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(v.y) : "h"(static_cast<uint16_t>(c.x >> 16)));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(v.z) : "h"(static_cast<uint16_t>(c.y)));
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(v.w) : "h"(static_cast<uint16_t>(c.y >> 16)));
+    row[j] = v;
+  }
+}
+
 // Fused RMSNorm + FP8 prologue on the staged rows (the CTA holds all K of each of the M rows):
 // the rule of rmsnorm_fp8_quant (tf_rmsnorm.cuh) applied in shared memory. Pass 1 sums the
-// squares in fp64, pass 2 writes y = fp16(x * rstd) * weight in place and takes amax|y|, pass 3
-// replaces y by the exact fp16 value of its e4m3 code e4m3(y / scale). The GEMV then runs
+// squares in fp64, pass 2 writes -y = -(fp16(x * rstd) * weight) in place and takes amax|y|,
+// pass 3 replaces it by the exact fp16 value of y's e4m3 code e4m3(y / scale). The GEMV then runs
 // exactly as on rmsnorm_fp8_quant's (codes, scale) and multiplies y by scale[m] in fp32, so its
 // output is bit-identical to the two-kernel path. red: >= 3 * 8 * warps floats of scratch.
 __device__ __forceinline__ void norm_quant_staged(const GemvParams& p, uint4* xs, float* red,
@@ -390,71 +404,44 @@ __device__ __forceinline__ void norm_quant_staged(const GemvParams& p, uint4* xs
   for (int m = 0; m < p.M; ++m) {
     const uint4* row = xs + (m * p.xs_stride) / 8;
     double s = 0.0;
-    for (int j = tid; j < nvec; j += nt) {
-      const uint4 v = row[j];
-      const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h[e]);
-        s += static_cast<double>(__fmul_rn(f.x, f.x)) + static_cast<double>(__fmul_rn(f.y, f.y));
-      }
-    }
+    for (int j = tid; j < nvec; j += nt) acc_sumsq(row[j], s);
     s = warp_sum(s);
     if (lane == 0) sh_sum[m * nw + warp] = s;
   }
   __syncthreads();
+  // Pass 2 leaves -y in the staging buffer (the form quant_vec divides); pass 3 replaces it by
+  // the fp16 value of y's e4m3 code, on the FMA division path when the row's |y| are finite.
   for (int m = 0; m < p.M; ++m) {
     double tot = 0.0;
     for (int w = 0; w < nw; ++w) tot += sh_sum[m * nw + w];
     const float rstd = rstd_of(tot, p.K, p.norm_eps);
+    const uint64_t rstd2 = f32x2(rstd, rstd);
     uint4* row = xs + (m * p.xs_stride) / 8;
-    float amax = 0.f;
-    for (int j = tid; j < nvec; j += nt) {
-      uint4 v = row[j];
-      const uint4 g = __ldg(wv + j);
-      __half2* h = reinterpret_cast<__half2*>(&v);
-      const __half2* g2 = reinterpret_cast<const __half2*>(&g);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h[e]);
-        const __half2 n2 = __halves2half2(__float2half_rn(__fmul_rn(f.x, rstd)),
-                                          __float2half_rn(__fmul_rn(f.y, rstd)));
-        h[e] = __hmul2(n2, g2[e]);
-        const float2 y = __half22float2(h[e]);
-        amax = fmaxf(amax, fmaxf(fabsf(y.x), fabsf(y.y)));
-      }
-      row[j] = v;
-    }
-    amax = warp_max(amax);
+    __half2 a2 = __float2half2_rn(0.f);
+    for (int j = tid; j < nvec; j += nt)
+      row[j] = norm_vec_neg(row[j], neg_weight(__ldg(wv + j)), rstd2, a2);
+    const float amax = warp_max(amax_of(a2));
     if (lane == 0) sh_max[m * nw + warp] = amax;
   }
   __syncthreads();
   for (int m = 0; m < p.M; ++m) {
+    float mx = 0.f;
+    for (int w = 0; w < nw; ++w) mx = fmaxf(mx, sh_max[m * nw + w]);
     float scale;
     if (p.norm_static != nullptr) {
       scale = __ldg(p.norm_static);
     } else {
-      float mx = 0.f;
-      for (int w = 0; w < nw; ++w) mx = fmaxf(mx, sh_max[m * nw + w]);
       scale = dyn_scale(mx);
       if (tid == 0 && p.norm_scale_out != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
         p.norm_scale_out[m] = scale;
     }
     if (tid == 0) scale_sh[m] = scale;
+    const Fp8Div d = fp8_div(scale);
+    const int path = quant_path(d, mx <= 65504.f, p.norm_static == nullptr);
     uint4* row = xs + (m * p.xs_stride) / 8;
-    for (int j = tid; j < nvec; j += nt) {
-      uint4 v = row[j];
-      uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 y = __half22float2(u32_as_h2(u[e]));
-        const uint16_t code = cvt_e4m3x2(__fdiv_rn(y.x, scale), __fdiv_rn(y.y, scale));
-        uint32_t h;
-        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(code));
-        u[e] = h;
-      }
-      row[j] = v;
-    }
+    if (path == kFma1) quant_staged<kFma1>(row, nvec, tid, nt, d);
+    else if (path == kFma2) quant_staged<kFma2>(row, nvec, tid, nt, d);
+    else quant_staged<kIeee>(row, nvec, tid, nt, d);
   }
   __syncthreads();
 }

@@ -480,3 +480,33 @@ def cast_e4m3(values: torch.Tensor) -> torch.Tensor:
         status = _lib.lib().tf_cast_e4m3(v.data_ptr(), v.numel(), out.data_ptr(), _lib.stream_ptr(v.device))
     _lib.check("tf_cast_e4m3", status)
     return out
+
+
+def e4m3_quant_rows(y: torch.Tensor, scale: torch.Tensor | None = None
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+    """e4m3(clamp(y / scale, -448, 448)) of fp16 activations [R, C] already normalised: the
+    quantization step of ``rmsnorm_fp8_quant`` on its own (C ABI ``tf_e4m3_quant_rows``).
+    ``scale``: one static fp32 value, one per row ([R] or [R, 1]), or None for the dynamic
+    per-row scale max(amax / 448, 1 / (448 * 512)). Returns (codes, scale [R, 1] or the given
+    scale)."""
+    _require(y, "y")
+    if y.dim() != 2 or y.dtype != torch.float16 or y.stride(1) != 1:
+        raise ValueError(f"y must be fp16 [R, C] with unit stride along C, got {y.dtype} "
+                         f"{tuple(y.shape)}")
+    r, c = y.shape
+    out = torch.empty((r, c), dtype=torch.float8_e4m3fn, device=y.device)
+    ldy = y.stride(0) if r > 1 else c
+    if scale is None:
+        sc, stride = None, 0
+        s_out = torch.empty((r, 1), dtype=torch.float32, device=y.device)
+    else:
+        sc = scale.reshape(-1)
+        if sc.dtype != torch.float32 or sc.device != y.device or sc.numel() not in (1, r):
+            raise ValueError(f"scale must be fp32 on {y.device} with 1 or {r} elements")
+        sc, stride, s_out = sc.contiguous(), 0 if sc.numel() == 1 else 1, scale
+    with torch.cuda.device(y.device):
+        status = _lib.lib().tf_e4m3_quant_rows(
+            y.data_ptr(), r, c, ldy, _lib.ptr(sc), stride, out.data_ptr(),
+            s_out.data_ptr() if scale is None else None, _lib.stream_ptr(y.device))
+    _lib.check("tf_e4m3_quant_rows", status)
+    return out, s_out
