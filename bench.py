@@ -920,6 +920,9 @@ def main() -> None:
                     help="restrict the sweep to these layer types (profiling a small case)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers in the sweep (28 = Qwen2.5-7B; fewer for a small case)")
+    ap.add_argument("--aux", action="store_true",
+                    help="run the AWQ repack and RMSNorm+FP8 legs with a restricted sweep too "
+                         "(profiling them on a small case)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warmup must be >= 3", file=sys.stderr)
@@ -1021,7 +1024,7 @@ def main() -> None:
         gemm = gemm_metric(device, tuple(sorted(gemm_ms)),
                            max(3, args.steps // 2), 3, pk, src, headline_m=args.gemm_m)
     extra = {}
-    if world == 1 and full and not args.skip_aux:
+    if world == 1 and (full or args.aux) and not args.skip_aux:
         extra["repack"] = repack_metric(device, max(3, args.steps // 2), pk)
         extra["rmsnorm_fp8"] = rmsnorm_metric(device, max(3, args.steps // 2), pk)
     block = None
