@@ -26,6 +26,7 @@ struct LinearPlan {
   int blocks_per_split;  // K blocks per split: 256 wide (GEMV), 128 (MMA tiles), 64 (tcgen05)
   unsigned grid_x, grid_y, grid_z;
   size_t workspace;      // bytes of scratch the launch needs
+  int stream_k;          // tcgen05 GEMM: stages dealt evenly over persistent CTAs (split_k 1)
 };
 
 // Fills `plan` for y[M, N] = x[M, K] * W[N, K]^T. Returns TF_OK or an error status.

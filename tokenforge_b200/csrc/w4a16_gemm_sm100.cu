@@ -110,6 +110,13 @@ struct TcParams {
   __half* y;
   int64_t ldy;
   float* partial;
+  // Stream-K (stream_k != 0): CTA c takes stages [c * stages_per_cta, (c + 1) * stages_per_cta)
+  // of the (n-tile, m-tile, K stage) sequence; a tile split across CTAs is summed by the last
+  // of them to finish (tickets: one counter per tile, zero at launch) from fp32 partials, two
+  // slots per CTA ([slot][BM tokens][128 rows]) in `partial`.
+  int stream_k;
+  int64_t stages_per_cta, total_stages;
+  uint32_t* tickets;
 };
 
 // ----------------------------------------------------------------------------- PTX wrappers
@@ -221,6 +228,8 @@ __device__ __forceinline__ constexpr uint32_t instr_desc() {
 struct Unit {
   int64_t n0;
   int m_tile, ks, kb0, kb1;
+  int tile;    // n-tile * m_tiles + m-tile
+  bool split;  // stream-K: part of a tile whose other stages belong to other CTAs
 };
 
 __device__ __forceinline__ Unit decode_unit(int u, const TcParams& p) {
@@ -234,6 +243,54 @@ __device__ __forceinline__ Unit decode_unit(int u, const TcParams& p) {
   w.kb0 = w.ks * p.kb_per_split;
   w.kb1 = min(p.kb_total, w.kb0 + p.kb_per_split);
   return w;
+}
+
+// The work of one CTA, in the same order for every warp role: round-robin units (u = blockIdx.x,
+// + gridDim.x, ...) or, with stream-K, the pieces of its contiguous stage range.
+struct WorkIter {
+  int64_t pos, end;
+};
+
+__device__ __forceinline__ WorkIter work_begin(const TcParams& p) {
+  WorkIter it;
+  if (p.stream_k) {
+    it.pos = static_cast<int64_t>(blockIdx.x) * p.stages_per_cta;
+    it.end = min(p.total_stages, it.pos + p.stages_per_cta);
+  } else {
+    it.pos = blockIdx.x;
+    it.end = p.units;
+  }
+  return it;
+}
+
+__device__ __forceinline__ bool work_next(const TcParams& p, WorkIter& it, Unit& w) {
+  if (it.pos >= it.end) return false;
+  if (!p.stream_k) {
+    w = decode_unit(static_cast<int>(it.pos), p);
+    w.tile = static_cast<int>(it.pos);
+    w.split = false;
+    it.pos += gridDim.x;
+    return true;
+  }
+  const int64_t t = it.pos / p.kb_total;
+  const int kb0 = static_cast<int>(it.pos - t * p.kb_total);
+  const int64_t room = kb0 + (it.end - it.pos);
+  const int kb1 = room < p.kb_total ? static_cast<int>(room) : p.kb_total;
+  w.tile = static_cast<int>(t);
+  w.m_tile = static_cast<int>(t % p.m_tiles);
+  w.n0 = (t / p.m_tiles) * kBlockN;
+  w.ks = 0;
+  w.kb0 = kb0;
+  w.kb1 = kb1;
+  w.split = !(kb0 == 0 && kb1 == p.kb_total);
+  it.pos += kb1 - kb0;
+  return true;
+}
+
+// Stream-K partial slot of CTA c's piece of tile t: slot 2c for the piece that starts its
+// range, 2c + 1 for the piece that ends it (a CTA whose range lies inside one tile has one).
+__device__ __forceinline__ int64_t stream_slot(const TcParams& p, int64_t c, int64_t t) {
+  return 2 * c + (c * p.stages_per_cta >= t * p.kb_total ? 0 : 1);
 }
 
 template <int BM, int KB>
@@ -295,8 +352,9 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-        const Unit w = decode_unit(u, p);
+      WorkIter wi = work_begin(p);
+      Unit w;
+      while (ok && work_next(p, wi, w)) {
         const int m0 = w.m_tile * BM;
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const uint32_t s = it % SP, ph = (it / SP) & 1u;
@@ -328,8 +386,9 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
       bool ok = true;
       bool issued = false;
       uint32_t last_a = 0, last_aph = 0;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++tc) {
-        const Unit w = decode_unit(u, p);
+      WorkIter wi = work_begin(p);
+      Unit w;
+      for (; ok && work_next(p, wi, w); ++tc) {
         const uint32_t b = tc & 1u, aph = (tc >> 1) & 1u;
         if (!mbar_wait(&acc_empty[b], aph ^ 1u, kErrMmaAccEmpty)) {
           ok = false;
@@ -369,8 +428,9 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     const int q = warp - kEpiWarp0;  // TMEM lanes 32q .. 32q+31
     uint32_t tc = 0;
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tc) {
-      const Unit w = decode_unit(u, p);
+    WorkIter wi = work_begin(p);
+    Unit w;
+    for (; work_next(p, wi, w); ++tc) {
       const uint32_t b = tc & 1u, aph = (tc >> 1) & 1u;
       if (!mbar_wait(&acc_full[b], aph, kErrEpiAccFull)) break;
       tc_fence_after();
@@ -379,6 +439,10 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
       const bool n_ok = n < p.N;
       float bv = 0.f;
       if (n_ok && p.k_splits == 1 && p.bias != nullptr) bv = __half2float(p.bias[n]);
+      // Stream-K piece: the whole [BM x 128] fp32 tile goes to this CTA's slot, row-contiguous
+      // per token so that a warp's 32 rows are one 128-byte segment.
+      float* slot = w.split ? p.partial + stream_slot(p, blockIdx.x, w.tile) * (BM * kBlockN)
+                            : nullptr;
       constexpr int kChunk = BM < 32 ? 16 : 32;
 #pragma unroll 1
       for (int c0 = 0; c0 < BM; c0 += kChunk) {
@@ -389,7 +453,11 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
         else
           tmem_ld_16cols(taddr, r);
         tmem_ld_wait();
-        if (n_ok) {
+        if (w.split) {
+#pragma unroll
+          for (int j = 0; j < kChunk; ++j)
+            __stcg(slot + (c0 + j) * kBlockN + 32 * q + lane, __uint_as_float(r[j]));
+        } else if (n_ok) {
 #pragma unroll
           for (int j = 0; j < kChunk; ++j) {
             const int64_t m = m0 + c0 + j;
@@ -406,6 +474,47 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (w.split) {
+        // The last CTA to finish its piece of this tile sums the pieces' rows 32q .. 32q+31 in
+        // stage order (deterministic whatever the arrival order), adds the bias and writes y.
+        // One ticket per (tile, warp quarter): no warp waits on another.
+        __threadfence();
+        __syncwarp();
+        uint32_t ticket = 0;
+        if (lane == 0) ticket = atomicAdd(p.tickets + 4 * static_cast<int64_t>(w.tile) + q, 1u);
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        const int64_t c_first = static_cast<int64_t>(w.tile) * p.kb_total / p.stages_per_cta;
+        const int64_t c_last =
+            (static_cast<int64_t>(w.tile + 1) * p.kb_total - 1) / p.stages_per_cta;
+        if (ticket == static_cast<uint32_t>(c_last - c_first)) {
+          __threadfence();
+          if (n_ok) {
+            const float bias_v = p.bias != nullptr ? __half2float(p.bias[n]) : 0.f;
+            // 16 tokens at a time: each piece's 16 values are independent loads, so a piece
+            // costs one L2 round trip per 16 tokens.
+            constexpr int kFix = 16;
+#pragma unroll 1
+            for (int j0 = 0; j0 < BM && m0 + j0 < p.M; j0 += kFix) {
+              float acc[kFix];
+              const float* src0 = p.partial + stream_slot(p, c_first, w.tile) * (BM * kBlockN) +
+                                  j0 * kBlockN + 32 * q + lane;
+#pragma unroll
+              for (int j = 0; j < kFix; ++j) acc[j] = __ldcg(src0 + j * kBlockN);
+              for (int64_t c = c_first + 1; c <= c_last; ++c) {
+                const float* src = p.partial + stream_slot(p, c, w.tile) * (BM * kBlockN) +
+                                   j0 * kBlockN + 32 * q + lane;
+#pragma unroll
+                for (int j = 0; j < kFix; ++j) acc[j] += __ldcg(src + j * kBlockN);
+              }
+#pragma unroll
+              for (int j = 0; j < kFix; ++j) {
+                const int64_t m = m0 + j0 + j;
+                if (m < p.M) p.y[m * p.ldy + n] = __float2half_rn(acc[j] + bias_v);
+              }
+            }
+          }
+        }
+      }
     }
   } else if (warp >= kDeqWarp0 && warp < kDeqWarp0 + kDeq) {
     const int d = warp - kDeqWarp0;
@@ -417,8 +526,9 @@ __global__ void __launch_bounds__(cta_threads<BM>(), 1)
     const int nib = 4 * awq_nibble_of(t & 7);
     uint32_t it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
-      const Unit w = decode_unit(u, p);
+    WorkIter wi = work_begin(p);
+    Unit w;
+    while (ok && work_next(p, wi, w)) {
       for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
         const uint32_t s = it % SP, ph = (it / SP) & 1u;
         const uint32_t a = it % SA, aph = (it / SA) & 1u;
@@ -555,6 +665,23 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
   p.y = reinterpret_cast<__half*>(a.y);
   p.ldy = a.ldy;
   p.partial = pl.split_k > 1 ? static_cast<float*>(a.workspace) : nullptr;
+  p.stream_k = pl.stream_k;
+  p.stages_per_cta = pl.blocks_per_split;
+  p.total_stages = static_cast<int64_t>(p.units) * p.kb_total;
+  p.tickets = nullptr;
+  if (pl.stream_k) {
+    // Stream-K: the tickets (one per tile and 32-row quarter) follow the partial slots and must
+    // read zero when the kernel starts.
+    const size_t partial = static_cast<size_t>(2 * pl.grid_x) * BM * kBlockN * sizeof(float);
+    p.partial = static_cast<float*>(a.workspace);
+    p.tickets = reinterpret_cast<uint32_t*>(static_cast<char*>(a.workspace) + partial);
+    const cudaError_t me = cudaMemsetAsync(p.tickets, 0, static_cast<size_t>(p.units) * 4 *
+                                                             sizeof(uint32_t), stream);
+    if (me != cudaSuccess) {
+      last_cuda_error() = static_cast<int>(me);
+      return TF_ERR_CUDA;
+    }
+  }
 
   static std::once_flag attr_once[64];
   int dev = 0;
@@ -570,7 +697,7 @@ int launch_bm(const LinearPlan& pl, const LinearArgs& a, cudaStream_t stream) {
   }
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min(p.units, num_sms())));
+  cfg.gridDim = dim3(pl.stream_k ? pl.grid_x : static_cast<unsigned>(std::min(p.units, num_sms())));
   cfg.blockDim = dim3(cta_threads<BM>());
   cfg.dynamicSmemBytes = L::kSmemBytes;
   cfg.stream = stream;
@@ -611,6 +738,31 @@ void plan_tc(int64_t M, int64_t N, int64_t K, LinearPlan* pl) {
   const int64_t kb = K / stage_k;
   const int64_t min_per = 8 * kBlockK / stage_k;  // at least 512 of K per split
   const int sms = 148;
+  pl->stream_k = 0;
+  // Tiles that do not divide over the SMs (o and down, N = 3584: 28 n-tiles) are dealt as
+  // stream-K: every persistent CTA takes the same number of K stages of the tile sequence, and a
+  // tile cut between CTAs is summed by the last of them (fp32 partials, two slots per CTA).
+  // Only where a CTA's run covers at least half a tile (a tile is cut into at most about three
+  // pieces); with shorter runs the last CTA's sum of many pieces costs more than the split-K
+  // reduce launch it replaces.
+  const int64_t sk_total = base * kb;
+  const int64_t sk_per = cdiv(sk_total, sms);
+  if (static_cast<double>(cdiv(base, sms)) > 1.05 * static_cast<double>(base) / sms &&
+      2 * sk_per >= kb) {
+    const int64_t grid = cdiv(sk_total, sk_per);
+    pl->stream_k = 1;
+    pl->split_k = 1;
+    pl->cluster = 1;
+    pl->blocks_per_split = static_cast<int>(sk_per);
+    pl->tile_n = kBlockN;
+    pl->warps_k = 1;
+    pl->grid_x = static_cast<unsigned>(grid);
+    pl->grid_y = 1;
+    pl->grid_z = 1;
+    const size_t partial = static_cast<size_t>(2 * grid) * pl->tile_m * kBlockN * sizeof(float);
+    pl->workspace = partial + static_cast<size_t>(base) * 4 * sizeof(uint32_t);
+    return;
+  }
   int best_s = 1;
   double best = static_cast<double>(cdiv(base, sms));
   for (int s = 2; s <= 8; ++s) {
