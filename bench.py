@@ -530,6 +530,65 @@ def decode_parity(device: torch.device, rank: int, world: int, peers, m: int) ->
     return res
 
 
+def peer_trace_leg(device: torch.device, rank: int, world: int, peers, m: int,  # type: ignore[no-untyped-def]
+                   reps: int = 20) -> dict:
+    """Where the fused all-reduce GEMV spends its time (N > 1; tf_peer_trace): for o and down of
+    Qwen2.5-7B, `reps` times, eight back-to-back fused calls of the layer with the last one
+    traced. Every 32-row tile's storing warp stamps %globaltimer at the exchange's entry (its
+    partial sums done), after its stores to every peer, when the last peer word has arrived, and
+    after writing y. The eight calls are one CUDA graph (the last captured with the trace
+    buffer), so the traced launch runs in a device-side stream of exchanges, as in the sweep.
+    Reported in us, medians over the replays:
+      entry_spread: last tile's entry minus first tile's entry on this rank (compute imbalance);
+      store: entry -> stores issued; wait: stores issued -> last peer word here (median tile,
+      and the slowest tile); tail: arrived -> y written.
+    The GPUs' timers are not aligned with each other (offsets of seconds were seen), so skew
+    between ranks shows only inside `wait` (the peer's matching tile stored later, plus the
+    store's flight over NVLink). The timer ticks in 256 ns steps on this B200 pool."""
+    import torch.distributed as dist
+
+    from tokenforge_b200 import _lib, tp
+
+    gen = torch.Generator(device=device).manual_seed(2028)
+    lib = _lib.lib()
+    out: dict[str, object] = {"m": m, "reps": reps}
+    for name, n, k in (("o", HIDDEN, HIDDEN), ("down", HIDDEN, INTER)):
+        w = random_w4a16(n, k, gen, device)
+        x = torch.randn((m, k), generator=gen, device=device).to(torch.float16)
+        shard = tp.shard_layer(w, "row", rank, world)
+        tiles = -(-n // 32)
+        rec = torch.zeros(4 * tiles, dtype=torch.int64, device=device)
+
+        def calls() -> None:
+            for i in range(8):
+                if i == 7:
+                    lib.tf_peer_trace(ctypes.c_void_p(rec.data_ptr()))
+                tp.linear_shard(x, shard, peers=peers)
+                if i == 7:
+                    lib.tf_peer_trace(None)
+
+        for _ in range(3):
+            tp.linear_shard(x, shard, peers=peers)
+        torch.cuda.synchronize(device)
+        graph = capture(calls, device)
+        rows = []
+        for _ in range(reps):
+            dist.barrier(device_ids=[device.index])
+            graph.replay()
+            torch.cuda.synchronize(device)
+            t = rec.view(tiles, 4).cpu().double()
+            first = t[:, 0].min()
+            rows.append([float(t[:, 0].max() - first), float((t[:, 1] - t[:, 0]).median()),
+                         float((t[:, 2] - t[:, 1]).median()), float((t[:, 2] - t[:, 1]).max()),
+                         float((t[:, 3] - t[:, 2]).median())])
+        del graph
+        med = torch.tensor(rows).median(dim=0).values.tolist()
+        keys = ("entry_spread", "store", "wait", "wait_max", "tail")
+        out[name] = {kk: round(v / 1e3, 3) for kk, v in zip(keys, med)}
+        del w, shard
+    return out
+
+
 def e2e_graph(sweep: DecodeSweep, device: torch.device, steps: int, barrier, world: int) -> dict:  # type: ignore[no-untyped-def]
     """The sweep end to end through the C ABI, as a user serves it: every step copies the step's
     activations from pinned host memory to the device, runs the 112 tf_w4a16_linear calls (plus
@@ -920,6 +979,8 @@ def main() -> None:
                     help="restrict the sweep to these layer types (profiling a small case)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers in the sweep (28 = Qwen2.5-7B; fewer for a small case)")
+    ap.add_argument("--peer-trace", action="store_true",
+                    help="N > 1: trace the fused all-reduce's exchange on o and down (peer_trace)")
     ap.add_argument("--aux", action="store_true",
                     help="run the AWQ repack and RMSNorm+FP8 legs with a restricted sweep too "
                          "(profiling them on a small case)")
@@ -1014,6 +1075,8 @@ def main() -> None:
     e2e_value = total_bytes / (e2e["ms_per_step"] * 1e-3) / 1e9
     # Correctness of the timed paths at this N (fused all-reduce across ranks at N > 1).
     parity = decode_parity(device, rank, world, peers, min(args.m, 8))
+    peer_trace = (peer_trace_leg(device, rank, world, peers, min(args.m, 8))
+                  if args.peer_trace and world > 1 and peers is not None else None)
     chain = None
     if world == 1 and full and not args.skip_chain and args.m <= 8:
         chain = chain_leg(sweep, device, args.steps)
@@ -1090,6 +1153,7 @@ def main() -> None:
                     "path": "tf_w4a16_linear C ABI calls with pinned H2D / D2H copies, the step "
                             "captured as one CUDA graph and replayed per step"},
             "parity": parity,
+            **({"peer_trace": peer_trace} if peer_trace else {}),
             "chain": chain,
             "gpu_launches": sweep.launches_per_step * args.steps,
             "clocks": clocks.summary(),

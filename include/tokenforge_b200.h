@@ -265,6 +265,14 @@ TF_API int tf_w4a16_linear_allreduce(const uint16_t* x, int64_t M, int64_t K, in
                     uint16_t* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                     const TfPeerSet* peers, void* stream);
 
+/* Tracing of the fused all-reduce (no reference counterpart): from the next call of
+ * tf_w4a16_linear_allreduce on, in this process, each 32-row tile's storing warp writes four
+ * %globaltimer stamps (ns) to records[4 * tile .. 4 * tile + 3]: entry to the exchange (its
+ * partial sums done), its stores to every peer issued, the last peer word arrived, y written.
+ * records: device memory of 4 * ceil(N / 32) uint64 on the calling device; NULL turns it off.
+ * A launch captured in a CUDA graph keeps the pointer it was captured with. */
+TF_API int tf_peer_trace(uint64_t* records);
+
 /* Launch-table introspection (replaces config.default_config / GemmConfig, config.py:23-92).
  * Writes the launch chosen for (M, N, K, G) into out[0..8]:
  *   {kernel (0 = gemv, 1 = mma gemm, 2 = tcgen05 gemm), m_bucket, tile_n, warps_k, split_k,

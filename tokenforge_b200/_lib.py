@@ -82,6 +82,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tf_peer_mailbox_close": (ctypes.c_int, [_P]),
     "tf_peer_mailbox_free": (ctypes.c_int, [_P]),
     "tf_peer_mailbox_error": (ctypes.c_int, [_P, _P]),
+    "tf_peer_trace": (ctypes.c_int, [_P]),
     "tf_w4a16_linear_allreduce": (
         ctypes.c_int,
         [_P, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _SZ, _P, _P],

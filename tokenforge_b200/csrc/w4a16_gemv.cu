@@ -36,6 +36,8 @@
 // the CTAs of a thread-block cluster (rank 0 sums the ranks' partials through distributed shared
 // memory in rank order): deterministic, no workspace, no second launch. CTAs that split K beyond
 // one cluster write fp32 partials that a second kernel reduces in split order.
+#include <atomic>
+
 #include "tf_common.cuh"
 #include "tf_plan.h"
 #include "tf_rmsnorm.cuh"
@@ -43,6 +45,9 @@
 
 namespace tfb {
 namespace {
+
+// Device buffer that fused all-reduce launches stamp (tf_peer_trace), or null.
+std::atomic<uint64_t*> g_peer_trace{nullptr};
 
 constexpr int kCtaWarps = 8;     // warps per CTA (WARPS_N x WARPS_K), two CTAs per SM ...
 constexpr int kWideWarps = 16;   // ... or one 16-warp CTA per SM splitting K 16 ways
@@ -75,6 +80,7 @@ struct GemvParams {
   int peer_participants;                  // storing warps of the grid (one per 32-row tile)
   uint32_t* peer_ctl;                     // own mailbox header: call counter, arrivals, error
   uint64_t* peer_data[TF_MAX_PEERS];       // rank q's tagged partials [2][world][max_m][max_n]
+  uint64_t* peer_trace;  // optional: per storing warp {entry, stored, arrived, done} globaltimer ns
   // Fused RMSNorm + FP8 prologue (kernels instantiated with kNorm): x is the un-normalised fp16
   // input, norm_w the RMSNorm weight [K]; every CTA covers the whole row.
   const __half* norm_w;
@@ -140,6 +146,7 @@ constexpr uint64_t kPeerWaitNs = 2000000000ull;  // give up on a silent peer aft
 // which the peer writes only after its previous call (and its reads) ended. Tags are call + 1.
 __device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (&v)[2][4], int rr,
                                               int c, int lane, uint32_t call) {
+  const uint64_t t_entry = p.peer_trace != nullptr ? globaltimer_ns() : 0;
   const int W = p.peer_world, me = p.peer_rank;
   const int par = static_cast<int>(call & 1u);
   const uint32_t tag = call + 1u;
@@ -169,6 +176,7 @@ __device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (
   // Sum in rank order. Words are requested in batches of independent loads (all of the lane's
   // words of the one peer when world == 2; else, per tile, the words of all peers), so a batch
   // costs one round trip; only words whose tag is not yet the call's are polled again.
+  const uint64_t t_stored = p.peer_trace != nullptr ? globaltimer_ns() : 0;
   const uint64_t* mine = p.peer_data[me] + static_cast<size_t>(par) * W * slot;
   bool timed_out = false;
   const uint64_t t0 = globaltimer_ns();
@@ -247,6 +255,11 @@ __device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (
       }
     }
   }
+  uint64_t t_arrived = 0;
+  if (p.peer_trace != nullptr) {
+    __syncwarp();
+    t_arrived = globaltimer_ns();
+  }
 #pragma unroll
   for (int t = 0; t < 2; ++t)
 #pragma unroll
@@ -254,6 +267,16 @@ __device__ __forceinline__ void peer_exchange(const GemvParams& p, const float (
       const int n = rr + 2 * t + (r >> 1), m = 2 * c + (r & 1);
       if (live[t][r]) p.y[m * p.ldy + n] = __float2half_rn(sum[t][r]);
     }
+  if (p.peer_trace != nullptr) {
+    __syncwarp();
+    if (lane == 0) {
+      uint64_t* rec = p.peer_trace + 4 * static_cast<size_t>(rr / kWarpRows);
+      rec[0] = t_entry;
+      rec[1] = t_stored;
+      rec[2] = t_arrived;
+      rec[3] = globaltimer_ns();
+    }
+  }
   if (timed_out) atomicCAS(p.peer_ctl + 2, 0u, 1u);
   __syncwarp();
   if (lane == 0) {
@@ -889,6 +912,7 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
   p.peer_world = 0;
   p.peer_rank = 0;
   p.peer_ctl = nullptr;
+  p.peer_trace = nullptr;
   p.norm_w = reinterpret_cast<const __half*>(a.norm_w);
   p.norm_eps = a.norm_eps;
   p.norm_static = a.norm_static;
@@ -902,6 +926,7 @@ int launch_gemv(const LinearPlan& plan, const LinearArgs& a, cudaStream_t stream
     p.peer_max_n = ps.max_n;
     p.peer_participants = static_cast<int>(plan.grid_x) * gemv_warps_n(plan.warps_k);
     p.peer_ctl = static_cast<uint32_t*>(ps.mailbox[ps.rank]);
+    p.peer_trace = g_peer_trace.load();
     for (int q = 0; q < TF_MAX_PEERS; ++q) {
       char* base = q < ps.world ? static_cast<char*>(ps.mailbox[q]) : nullptr;
       p.peer_data[q] = base ? reinterpret_cast<uint64_t*>(base + lay.data_off) : nullptr;
@@ -954,3 +979,11 @@ int launch_splitk_reduce(const float* partial, int split, int64_t M, int64_t N,
 }
 
 }  // namespace tfb
+
+// Peer-exchange tracing of the fused all-reduce GEMV (see the header): later launches of
+// tf_w4a16_linear_allreduce in this process stamp `records` (device memory, 4 uint64 per 32-row
+// tile of the layer, indexed by tile), or nothing when it is null.
+extern "C" int tf_peer_trace(uint64_t* records) {
+  tfb::g_peer_trace.store(records);
+  return TF_OK;
+}
