@@ -41,6 +41,8 @@ def _weights(n: int, k: int, seed: int) -> tuple[W4A16Weights, torch.Tensor]:
     (3584, 18944, (1024, 2048)),  # down
     (3584, 3584, (1024, 3000)),   # o
     (3584, 7168, (1024, 1500)),
+    (3584, 512, (2048,)),         # o's K shard at TP 8 (tiles of 8 stages)
+    (3584, 384, (2048,)),
 ])
 def test_stream_k_tiles_match_fp64_and_repeat_bit_identically(
         n: int, k: int, ms: tuple[int, ...], device: torch.device) -> None:
@@ -58,7 +60,10 @@ def test_stream_k_tiles_match_fp64_and_repeat_bit_identically(
                                                   "cuda")
             want = ref if b is None else ref + b.to(torch.float64)
             err = float((y.to(torch.float64) - want).abs().max())
-            assert err <= tol, f"N={n} K={k} M={m} bias={b is not None}: {err:.3e} > {tol:.3e}"
+            # The reference's rule scales with sqrt(K); at K = 384-512 it falls below the fp16
+            # rounding of the largest outputs (|y| ~ 10), so half an ulp of max|y| is added.
+            bound = tol + float(want.abs().max()) * 2.0**-11
+            assert err <= bound, f"N={n} K={k} M={m} bias={b is not None}: {err:.3e} > {bound:.3e}"
             again = torch.ops.tokenforge.w4a16_linear(x, wd.qweight_t, wd.scales, wd.qzeros, b, G,
                                                       "cuda")
             assert torch.equal(y, again), f"N={n} K={k} M={m}: repeated call differs"
