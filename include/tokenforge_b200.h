@@ -116,8 +116,10 @@ TF_API int tf_w4a16_dequant(const int32_t* qweight_t, const uint16_t* scales, co
  * GEMM above.
  *
  * bias may be NULL. Workspace: tf_w4a16_workspace_bytes(M, N, K, group_size) bytes of device
- * memory (may be 0, then workspace may be NULL); contents need not be initialised; it must
- * not be used by another call that runs concurrently. */
+ * memory (may be 0, then workspace may be NULL); contents need not be initialised (the
+ * tensor-core GEMM's stream-K plans clear their ticket area with a cudaMemsetAsync on the
+ * call's stream before the kernel); it must not be used by another call that runs
+ * concurrently. */
 TF_API size_t tf_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t group_size);
 
 TF_API int tf_w4a16_gemv(const uint16_t* x, int64_t M, int64_t K, int64_t ldx,
