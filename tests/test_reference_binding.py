@@ -20,7 +20,8 @@ from pathlib import Path
 import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
-REFERENCE = Path(os.environ.get("TOKENFORGE_REFERENCE", "/root/reference"))
+# The TokenForge checkout: $TOKENFORGE_REFERENCE, else a `reference` directory beside this repo.
+REFERENCE = Path(os.environ.get("TOKENFORGE_REFERENCE", str(ROOT.parent / "reference")))
 
 SCRIPT = textwrap.dedent(
     """
